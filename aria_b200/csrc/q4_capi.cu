@@ -1,0 +1,147 @@
+// q4_capi.cu -- extern "C" entry points of libaria_q4.so (declared in
+// include/aria_q4.h).  Argument checking, status codes and kernel selection;
+// the kernels live in q4_pack.cu, q4_decode.cu and q4_gemm_tc.cu.
+#include <cstdio>
+
+#include "../../include/aria_q4.h"
+#include "q4_common.cuh"
+
+namespace aria_q4 {
+cudaError_t launch_pack_f16(const uint16_t* src, size_t n, uint8_t* dst, cudaStream_t st);
+cudaError_t launch_pack_f32(const float* src, size_t n, uint8_t* dst, cudaStream_t st);
+cudaError_t launch_unpack(const uint8_t* blocks, size_t n, float* dst, cudaStream_t st);
+cudaError_t launch_repack(const uint8_t* blocks, int layout, int K, int N, uint8_t* tiled, cudaStream_t st);
+cudaError_t launch_quantize_tiled(const uint16_t* w, int layout, int K, int N, uint8_t* tiled, cudaStream_t st);
+cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
+                          int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl);
+cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
+                           int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl);
+int take_device_error();
+}  // namespace aria_q4
+
+// M at or below which the register-fed decode kernel is used; above it the
+// tcgen05 kernel (each dequantised weight then serves up to 256 tokens).
+static const int kDecodeMaxM = 32;
+
+using namespace aria_q4;
+
+static thread_local int g_last_cuda_error = 0;
+
+static int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return ARIA_Q4_OK;
+  g_last_cuda_error = (int)e;
+  return ARIA_Q4_ECUDA;
+}
+
+// The library is built for sm_100a only; refuse to launch anywhere else.
+static int check_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  int major = 0, minor = 0;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (major != 10 || minor != 0) return ARIA_Q4_ENODEVICE;
+  return ARIA_Q4_OK;
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+static int check_tiled_shape(int layout, int K, int N) {
+  if (layout != ARIA_Q4_LAYOUT_KN && layout != ARIA_Q4_LAYOUT_NK) return ARIA_Q4_EINVAL;
+  if (K <= 0 || N <= 0) return ARIA_Q4_EINVAL;
+  if (K % kBlock != 0) return ARIA_Q4_EUNSUPPORTED;
+  if (layout == ARIA_Q4_LAYOUT_KN && N % kBlock != 0) return ARIA_Q4_EUNSUPPORTED;
+  if ((long long)K * (long long)N >= (1LL << 40)) return ARIA_Q4_EUNSUPPORTED;
+  return ARIA_Q4_OK;
+}
+
+extern "C" {
+
+size_t aria_q4_0_packed_bytes(size_t n) { return (n + kBlock - 1) / kBlock * kBlockBytes; }
+
+int aria_q4_0_pack_f16(const uint16_t* src, size_t n, uint8_t* dst, void* stream) {
+  if (n == 0) return ARIA_Q4_OK;
+  if (!src || !dst) return ARIA_Q4_EINVAL;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_pack_f16(src, n, dst, (cudaStream_t)stream));
+}
+
+int aria_q4_0_pack_f32(const float* src, size_t n, uint8_t* dst, void* stream) {
+  if (n == 0) return ARIA_Q4_OK;
+  if (!src || !dst) return ARIA_Q4_EINVAL;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_pack_f32(src, n, dst, (cudaStream_t)stream));
+}
+
+int aria_q4_0_unpack_f32(const uint8_t* blocks, size_t n, float* dst, void* stream) {
+  if (n == 0) return ARIA_Q4_OK;
+  if (!blocks || !dst) return ARIA_Q4_EINVAL;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_unpack(blocks, n, dst, (cudaStream_t)stream));
+}
+
+size_t aria_q4_0_tiled_bytes(int K, int N) {
+  if (K <= 0 || N <= 0) return 0;
+  return tiled_bytes(K, N);
+}
+
+int aria_q4_0_repack(const uint8_t* blocks, int layout, int K, int N, void* tiled, size_t tiled_bytes_,
+                     void* stream) {
+  if (int s = check_tiled_shape(layout, K, N)) return s;
+  if (!blocks || !tiled) return ARIA_Q4_EINVAL;
+  if (((uintptr_t)tiled & 255u) != 0) return ARIA_Q4_EALIGN;
+  if (tiled_bytes_ < tiled_bytes(K, N)) return ARIA_Q4_ESIZE;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_repack(blocks, layout, K, N, (uint8_t*)tiled, (cudaStream_t)stream));
+}
+
+int aria_q4_0_quantize_tiled(const uint16_t* w, int layout, int K, int N, void* tiled, size_t tiled_bytes_,
+                             void* stream) {
+  if (int s = check_tiled_shape(layout, K, N)) return s;
+  if (!w || !tiled) return ARIA_Q4_EINVAL;
+  if (((uintptr_t)tiled & 255u) != 0) return ARIA_Q4_EALIGN;
+  if (tiled_bytes_ < tiled_bytes(K, N)) return ARIA_Q4_ESIZE;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_quantize_tiled(w, layout, K, N, (uint8_t*)tiled, (cudaStream_t)stream));
+}
+
+int aria_q4_0_matmul(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
+                     int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, void* stream) {
+  if (int s = check_tiled_shape(layout, K, N)) return s;
+  if (M < 0) return ARIA_Q4_EINVAL;
+  if (M == 0) return ARIA_Q4_OK;
+  if (!tiled || !x || !y) return ARIA_Q4_EINVAL;
+  if (y_dtype != ARIA_Q4_F16 && y_dtype != ARIA_Q4_F32) return ARIA_Q4_EINVAL;
+  if (ldx < K || ldy < N) return ARIA_Q4_EINVAL;
+  if (((uintptr_t)tiled & 255u) != 0 || !aligned16(x) || (ldx % 8) != 0) return ARIA_Q4_EALIGN;
+  if (int s = check_device()) return s;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (M <= kDecodeMaxM)
+    return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
+                                     (const __half*)bias, alpha, beta, st, true));
+  return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
+                                    (const __half*)bias, alpha, beta, st, true));
+}
+
+const char* aria_q4_strerror(int status) {
+  switch (status) {
+    case ARIA_Q4_OK: return "ok";
+    case ARIA_Q4_EINVAL: return "invalid argument";
+    case ARIA_Q4_EUNSUPPORTED: return "unsupported shape (K must be a multiple of 32; N too for layout KN)";
+    case ARIA_Q4_EALIGN: return "misaligned pointer or leading dimension (x 16 B, ldx % 8, tiled 256 B)";
+    case ARIA_Q4_ECUDA: return "CUDA runtime error (see aria_q4_last_cuda_error)";
+    case ARIA_Q4_ENODEVICE: return "current device is not sm_100 (B200)";
+    case ARIA_Q4_ESIZE: return "destination buffer too small";
+    default: return "unknown status";
+  }
+}
+
+int aria_q4_last_cuda_error(void) { return g_last_cuda_error; }
+
+int aria_q4_take_device_error(void) { return take_device_error(); }
+int aria_q4_abi_version(void) { return ARIA_Q4_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,331 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Q4_0 projection path (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one Efkolos decode step at batch 1 -- the
+101 Q4_0 projections of a token (20 layers x QKV 896->2688, attn_out 896->896,
+ffn_up 896->3584, ffn_down 3584->896, plus the LM head 896->31500), launched in
+model order through the C ABI, each waiting on the previous (programmatic
+dependent launch), captured once in a CUDA graph per weight replica.  Metric:
+algorithmic HBM GB/s = (Q4_0 weight bytes + f16 activations in + f16 outputs
+out) / step time.  The weight set (124 MB) is as large as B200's L2, so steps
+rotate over weight replicas totalling > 4x L2; inputs are therefore never
+L2-resident between timed steps.
+
+Under torchrun (N > 1) every rank decodes its own sequence on a full weight
+replica (batch-sharded weak scaling, no data-path collective); value = bytes
+all ranks streamed / max-over-ranks time.
+
+--impl reference times the reference's CPU arithmetic for the same workload
+(dequantise + f32 matmul, the oracle restatement of transformer_cuda.rs:549-575
+and :3322-3333) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_0 GEMV HBM GB/s (decode)"
+UNIT = "GB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+        time.sleep(0.25)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+
+def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
+    """The reference's CPU arithmetic on a bounded sample of the decode step.
+
+    Sample: layer 0's four projections plus the LM head at M=1 (one fifth of the
+    layer work plus the whole head), Q4_0 blocks from the oracle packer,
+    dequantise + f32 matmul per call, repeated for about `seconds`."""
+    import numpy as np
+    from oracle.q4_oracle_np import COracle
+    from aria_b200.efkolos import EFKOLOS
+    orc = COracle()
+    threads = threads or os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    projs = [p for p in EFKOLOS.all_projections() if p[0].startswith("blk.0.") or p[0] == "lm_head"]
+    items = []
+    for (name, lay, K, N, s) in projs:
+        w = (rng.standard_normal(K * N, dtype=np.float32) * s).astype(np.float16)
+        blocks = orc.quantize_q4_0_f16(w)
+        x = rng.standard_normal((1, K)).astype(np.float16)
+        items.append((blocks, lay, K, N, x, np.zeros(K * N, np.float32), np.zeros(K, np.float32),
+                      np.zeros((1, N), np.float32)))
+    per_pass = sum(K * N // 32 * 18 + K * 2 + N * 2 for (_, _, K, N, _) in projs)
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        for (blocks, lay, K, N, x, ws, xs, y) in items:
+            orc.baseline_projection(blocks, lay, K, N, x, ws, xs, y, threads)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": per_pass * passes / el / 1e9, "unit": UNIT, "cores": threads,
+            "kind": "port", "seconds": el,
+            "sample": f"{passes} passes of layer-0 QKV/attn_out/ffn_up/ffn_down + LM head at M=1 "
+                      f"(dequantise + f32 i-p-j matmul, {threads} OpenMP threads)"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    # each step is one bounded sample; total stays within a few minutes
+    per_step = max(0.5, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_decode_sample(per_step / 4)
+    vals = [cpu_decode_sample(per_step) for _ in range(args.steps)]
+    v = statistics.median([r["value"] for r in vals])
+    cb = dict(vals[0])
+    cb["value"] = v
+    rec = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "efkolos_decode_b1 (BASELINE configs[1]), CPU sample", "M": 1},
+           "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(rec), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+    from aria_b200.efkolos import EFKOLOS, DecodeProgram, Q4Stack
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 2**20) or 126 * 2**20
+    cfg = EFKOLOS
+    stack0 = Q4Stack.build(cfg, seed=rank * 1000)
+    reps = max(2, -(-4 * l2 // stack0.nbytes) + 0)
+    stacks = [stack0] + [Q4Stack.build(cfg, seed=rank * 1000 + r) for r in range(1, reps)]
+    prog = DecodeProgram(stack0, M=1, seed=rank + 1)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(dev)
+    graphs = []
+    with torch.cuda.stream(stream):
+        for st in stacks:  # warm the path once outside capture
+            prog.run(st)
+        torch.cuda.synchronize()
+        for st in stacks:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                prog.run(st)
+            graphs.append(g)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def timed(fn, steps, warmup):
+        with torch.cuda.stream(stream):
+            for i in range(warmup):
+                fn(i)
+            torch.cuda.synchronize()
+            barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(steps):
+                fn(i)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    ms = timed(lambda i: graphs[i % reps].replay(), args.steps, args.warmup)
+    clocks = sampler.stop()
+    ms_step = ms / args.steps
+    bytes_step = prog.algorithmic_bytes()
+    value = bytes_step * world / (ms_step * 1e-3) / 1e9
+
+    # ---- dominant kernel: time each projection kind alone, chained like the step,
+    # rotating over copies of its weight that total > 4x L2 so no launch hits L2
+    from aria_b200.q4 import Q4Weight, matmul
+    kinds = {}
+    for idx, (name, w) in enumerate(stack0.weights):
+        kinds.setdefault(name.split(".")[-1], []).append(idx)
+    per_kind = {}
+    for kind, idxs in kinds.items():
+        w0 = stack0.weights[idxs[0]][1]
+        ncopy = max(4, -(-4 * l2 // w0.nbytes))
+        pool = [Q4Weight(w0.buf.clone(), w0.layout, w0.K, w0.N) for _ in range(ncopy)]
+        x_, y_ = prog.xs[idxs[0]], prog.ys[idxs[0]]
+        n_launch = max(64, min(512, ncopy))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            matmul(x_, pool[0], y_)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=stream):
+                for j in range(n_launch):
+                    matmul(x_, pool[j % ncopy], y_)
+        kms = timed(lambda i: g.replay(), 3, 2) / (3 * n_launch)
+        abytes = w0.nbytes + w0.K * 2 + w0.N * 2
+        per_kind[kind] = {"us_per_launch": round(kms * 1e3, 3), "launches_per_step": len(idxs),
+                          "share_est": kms * len(idxs), "alg_bytes": abytes,
+                          "gbs": abytes / (kms * 1e-3) / 1e9}
+        del g, pool
+        torch.cuda.empty_cache()
+    dom = max(per_kind, key=lambda k: per_kind[k]["share_est"])
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    roof = {"bound": "hbm", "kernel": f"gemv_kernel ({dom})", "achieved": per_kind[dom]["gbs"], "peak": hbm_peak,
+            "unit": "GB/s", "frac": per_kind[dom]["gbs"] / hbm_peak, "traffic": None,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
+            "per_kind": per_kind}
+
+    # ---- end to end through the public API with host buffers
+    x_host = torch.empty_like(prog.x_all, device="cpu").pin_memory()
+    x_host.copy_(prog.x_all)
+    out_host = torch.empty_like(prog.ys[-1], device="cpu").pin_memory()
+
+    def e2e_step(i):
+        prog.x_all.copy_(x_host, non_blocking=True)
+        graphs[i % reps].replay()
+        out_host.copy_(prog.ys[-1], non_blocking=True)
+
+    e2e_ms = timed(e2e_step, args.steps, args.warmup) / args.steps
+    e2e_val = bytes_step * world / (e2e_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_decode_sample(12.0)
+
+    rec = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "q4_0 weights, f16 activations, f32 accumulate", "data": "synthetic",
+           "config": {"workload": "efkolos_decode_b1 (BASELINE configs[1]): 20 layers x (QKV, attn_out, ffn_up, "
+                                  "ffn_down) + LM head, M=1, model-order chain",
+                      "M": 1, "weight_bytes": stack0.nbytes, "alg_bytes_per_step": bytes_step,
+                      "l2_policy": f"rotate {reps} weight replicas ({reps * stack0.nbytes / 2**20:.0f} MiB > 4x L2)",
+                      "parallelism": f"batch-sharded replicas x{world}"},
+           "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+           "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": prog.input_bytes(),
+                   "d2h_bytes_per_step": prog.ys[-1].numel() * 2, "ms_per_step": e2e_ms},
+           "gpu_launches": prog.launches * args.steps}
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    for g in graphs:
+        del g
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,125 @@
+/*
+ * aria_q4.h -- C ABI of the B200 (sm_100a) Q4_0 projection library, libaria_q4.so.
+ *
+ * Drop-in boundary for lold3344/ARIA's quantised inference path.  The reference
+ * binds its GPU work from Rust through cudarc: kernels by name from a PTX module
+ * (src/transformer_cuda.rs:832-890) and cuBLAS through the `gemm()` helper
+ * (src/transformer_cuda.rs:615-640).  These functions replace, for Q4_0
+ * weights, the five projection GEMMs and the CPU packer; a Rust `extern "C"`
+ * block for them is given in INTEGRATION.md.
+ *
+ * Conventions (all entry points):
+ *   - every pointer is a device pointer unless stated otherwise; `stream` is a
+ *     cudaStream_t (CUstream) passed as void*, NULL = legacy default stream;
+ *   - calls are stream-ordered and asynchronous: no host synchronisation, no
+ *     allocation, no global mutable state (safe on distinct streams/threads);
+ *   - the return value is an aria_q4_status; nothing aborts the process
+ *     (the reference unwraps and aborts on any CUDA error, Cargo.toml:24);
+ *   - layouts name the orientation of the reference's flat f16 tensor:
+ *       ARIA_Q4_LAYOUT_KN  w[k][n], blocks run along n: w_qkv [d][3d],
+ *                          w_out [d][d], w_ff1 [d][ff], w_ff2 [ff][d]
+ *                          (src/transformer_cuda.rs:263-270, gemm(..,false,false))
+ *       ARIA_Q4_LAYOUT_NK  w[n][k], blocks run along k: the tied LM head
+ *                          embed [V][d] (src/transformer_cuda.rs:314, :1864,
+ *                          gemm(..,false,true))
+ */
+#ifndef ARIA_Q4_H
+#define ARIA_Q4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ARIA_Q4_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define ARIA_Q4_API __attribute__((visibility("default")))
+#else
+#define ARIA_Q4_API
+#endif
+
+typedef enum {
+  ARIA_Q4_OK = 0,
+  ARIA_Q4_EINVAL = 1,       /* null pointer, negative size, bad enum value        */
+  ARIA_Q4_EUNSUPPORTED = 2, /* shape outside what the kernels handle (K % 32 etc.) */
+  ARIA_Q4_EALIGN = 3,       /* pointer or leading dimension not 16-byte aligned   */
+  ARIA_Q4_ECUDA = 4,        /* a CUDA runtime call failed: aria_q4_last_cuda_error */
+  ARIA_Q4_ENODEVICE = 5,    /* current device is not an sm_100 (B200) GPU          */
+  ARIA_Q4_ESIZE = 6         /* destination buffer smaller than required           */
+} aria_q4_status;
+
+enum { ARIA_Q4_LAYOUT_KN = 0, ARIA_Q4_LAYOUT_NK = 1 };
+/* element types, numbered like the reference's GGUF dtype ids (:2853, :3213) */
+enum { ARIA_Q4_F32 = 0, ARIA_Q4_F16 = 1 };
+
+/* ---------------------------------------------------------------- packer */
+
+/* Bytes of GGUF Q4_0 for n elements: ceil(n/32)*18 (src/transformer_cuda.rs:550-552). */
+ARIA_Q4_API size_t aria_q4_0_packed_bytes(size_t n);
+
+/* Replaces `quantize_q4_0(&[f32]) -> Vec<u8>` (src/transformer_cuda.rs:549-575) as
+ * called by push_q4! (:3214-3218) on a downloaded f16 weight: src is n f16 values,
+ * dst receives aria_q4_0_packed_bytes(n) bytes, identical to the Rust packer's. */
+ARIA_Q4_API int aria_q4_0_pack_f16(const uint16_t* src, size_t n, uint8_t* dst, void* stream);
+
+/* Same packer on an f32 buffer: the exact signature of quantize_q4_0 (&[f32]). */
+ARIA_Q4_API int aria_q4_0_pack_f32(const float* src, size_t n, uint8_t* dst, void* stream);
+
+/* Exact dequantisation (q-8)*scale of n elements of GGUF Q4_0 into f32.  The
+ * reference has no dequantiser (it never reads Q4_0 back, :3046-3065); this is
+ * the inverse its packer implies, used for checking and export round trips. */
+ARIA_Q4_API int aria_q4_0_unpack_f32(const uint8_t* blocks, size_t n, float* dst, void* stream);
+
+/* ---------------------------------------------------------------- device form */
+
+/* Bytes of the device-resident ("tiled") form of a K x N projection. */
+ARIA_Q4_API size_t aria_q4_0_tiled_bytes(int K, int N);
+
+/* Uploads a Q4_0 GGUF tensor into the tiled form.  Stands where the reference
+ * loader fills TransformerLayer.w_* / embed with f16 (load_f16!, :3046-3055),
+ * which cannot read dtype 2.  `blocks` = the tensor's K*N/32*18 bytes in the
+ * reference's flat order for `layout`.  Requires K % 32 == 0, and N % 32 == 0
+ * for KN.  tiled must be 256-byte aligned (cudaMalloc memory is). */
+ARIA_Q4_API int aria_q4_0_repack(const uint8_t* blocks, int layout, int K, int N,
+                     void* tiled, size_t tiled_bytes, void* stream);
+
+/* Quantises f16 weights (the reference's in-memory w_* / embed) straight into
+ * the tiled form, with the same bit-exact block quantiser as aria_q4_0_pack_*:
+ * repack(pack(w)) == quantize_tiled(w) byte for byte. */
+ARIA_Q4_API int aria_q4_0_quantize_tiled(const uint16_t* w, int layout, int K, int N,
+                             void* tiled, size_t tiled_bytes, void* stream);
+
+/* ---------------------------------------------------------------- projection */
+
+/* Replaces `gemm(blas, x, w, y, m, k, n, false, transb, alpha, beta)` followed
+ * by `add_bias` (src/transformer_cuda.rs:615-640 with :1583/:1686/:1753/:1805/
+ * :1864) when the weight is Q4_0:
+ *     y[m][n] = alpha * sum_k x[m][k] * W(k,n) + beta * y[m][n] + bias[n]
+ * W is the tiled form of the layout-oriented Q4_0 tensor (KN <=> transb=false,
+ * NK <=> transb=true).  x is f16 [M][ldx]; y is f16 or f32 (y_dtype) [M][ldy];
+ * bias (f16 [N]) may be NULL.  fp32 accumulation.  x must be 16-byte aligned
+ * with ldx % 8 == 0.  M >= 0; M == 0 is a no-op. */
+ARIA_Q4_API int aria_q4_0_matmul(const void* tiled, int layout, int K, int N,
+                     const uint16_t* x, int M, int ldx,
+                     void* y, int y_dtype, int ldy,
+                     const uint16_t* bias, float alpha, float beta, void* stream);
+
+/* ---------------------------------------------------------------- errors */
+
+ARIA_Q4_API const char* aria_q4_strerror(int status);
+/* cudaError_t of the last failing CUDA call on this thread (0 if none). */
+ARIA_Q4_API int aria_q4_last_cuda_error(void);
+/* Reads and clears the device-side error code of the current device: 0 = none,
+ * 1..3 = a bounded wait inside the tcgen05 kernel expired (the kernel returned
+ * without finishing its tile instead of hanging), -1 = the read failed.
+ * Synchronises the device.  No reference counterpart (the reference aborts). */
+ARIA_Q4_API int aria_q4_take_device_error(void);
+ARIA_Q4_API int aria_q4_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ARIA_Q4_H */

@@ -1,0 +1,67 @@
+"""CPU-side checks of the C ABI: the library loads, exports every declared
+symbol, and its pure-host functions answer without a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "aria_q4.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(aria_q4\w*)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from aria_b200 import _lib
+    return _lib.lib()
+
+
+def test_header_lists_functions():
+    names = declared_functions()
+    assert "aria_q4_0_matmul" in names and "aria_q4_0_pack_f16" in names
+    assert len(names) >= 10
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in aria_q4.h but not exported"
+
+
+def test_binding_covers_header():
+    from aria_b200._lib import SIGNATURES
+    assert set(SIGNATURES) == set(declared_functions())
+
+
+def test_host_only_functions(lib):
+    assert lib.aria_q4_abi_version() == 1
+    assert lib.aria_q4_0_packed_bytes(0) == 0
+    assert lib.aria_q4_0_packed_bytes(1) == 18
+    assert lib.aria_q4_0_packed_bytes(33) == 36
+    assert lib.aria_q4_0_packed_bytes(3584 * 896) == 1806336
+    assert lib.aria_q4_0_tiled_bytes(0, 5) == 0
+    K, N = 896, 2688
+    assert lib.aria_q4_0_tiled_bytes(K, N) >= K * N // 32 * 18
+    assert lib.aria_q4_strerror(0) == b"ok"
+    assert b"multiple of 32" in lib.aria_q4_strerror(2)
+
+
+def test_argument_errors_need_no_gpu(lib):
+    # shape / pointer validation happens before any CUDA call
+    P = ctypes.c_void_p
+    assert lib.aria_q4_0_matmul(P(256), 0, 33, 64, P(256), 1, 64, P(256), 1, 64, None, 1.0, 0.0, None) == 2
+    assert lib.aria_q4_0_matmul(P(256), 0, 64, 48, P(256), 1, 64, P(256), 1, 64, None, 1.0, 0.0, None) == 2
+    assert lib.aria_q4_0_matmul(P(256), 7, 64, 64, P(256), 1, 64, P(256), 1, 64, None, 1.0, 0.0, None) == 1
+    assert lib.aria_q4_0_matmul(None, 0, 64, 64, P(256), 1, 64, P(256), 1, 64, None, 1.0, 0.0, None) == 1
+    assert lib.aria_q4_0_matmul(P(256), 0, 64, 64, P(256), -1, 64, P(256), 1, 64, None, 1.0, 0.0, None) == 1
+    assert lib.aria_q4_0_matmul(P(256), 0, 64, 64, P(256), 0, 64, P(256), 1, 64, None, 1.0, 0.0, None) == 0
+    assert lib.aria_q4_0_matmul(P(256), 0, 64, 64, P(258), 1, 64, P(256), 1, 64, None, 1.0, 0.0, None) == 3
+    assert lib.aria_q4_0_repack(P(256), 1, 64, 64, P(256), 10, None) == 6
+    assert lib.aria_q4_0_repack(P(256), 1, 64, 64, P(260), 1 << 20, None) == 3
+    assert lib.aria_q4_0_pack_f16(None, 0, None, None) == 0
+    assert lib.aria_q4_0_pack_f16(None, 5, None, None) == 1

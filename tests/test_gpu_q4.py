@@ -1,0 +1,186 @@
+"""GPU parity tests: the CUDA kernels behind the C ABI against the CPU oracle.
+
+Bit-exact for packed bytes (lold3344/ARIA src/transformer_cuda.rs:549-575);
+projection outputs within max-abs 1e-2 and relative L2 1e-3 of the fp64
+dequantise-then-matmul reference (:3322-3333, :1864)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import q4_oracle_np as npo
+from tests.gpu_helpers import LAYOUT_KN, LAYOUT_NK, check_close, tiled_from_aos, tiled_regions
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
+
+
+@pytest.fixture(scope="module")
+def q4():
+    from aria_b200 import q4 as q4mod
+    return q4mod
+
+
+def _decode_input(case):
+    raw = bytes.fromhex(case["input_hex"])
+    if case["dtype"] == "f32":
+        return np.frombuffer(raw, dtype=">u4").astype("<u4").view(np.float32)
+    return np.frombuffer(raw, dtype=">u2").astype("<u2").view(np.float16)
+
+
+# ------------------------------------------------------------------ packer
+
+def test_pack_known_answers(q4, kat):
+    for case in kat:
+        x = _decode_input(case).copy()
+        got = q4.quantize_q4_0(torch.from_numpy(x).cuda()).cpu().numpy().tobytes().hex()
+        assert got == case["expected_hex"], case["name"]
+        if case["dtype"] == "f16":  # the f32 entry point on the widened values too
+            got32 = q4.quantize_q4_0(torch.from_numpy(x.astype(np.float32)).cuda()).cpu().numpy()
+            assert got32.tobytes().hex() == case["expected_hex"], case["name"] + " (f32)"
+
+
+@pytest.mark.parametrize("n", [1, 31, 32, 33, 32 * 1000 + 7, 3584 * 896, 896 * 2688 + 5])
+def test_pack_random_bit_exact(q4, coracle, n):
+    rng = np.random.default_rng(n)
+    w = (rng.standard_normal(n) * 0.02).astype(np.float16)
+    got = q4.quantize_q4_0(torch.from_numpy(w).cuda()).cpu().numpy()
+    ref = coracle.quantize_q4_0_f16(w)
+    assert got.size == ref.size == npo.packed_bytes(n)
+    assert np.array_equal(got, ref)
+
+
+def test_pack_f32_extremes_bit_exact(q4, coracle):
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal(32 * 4096) * np.float32(10.0) ** rng.integers(-40, 38, 32 * 4096)).astype(np.float32)
+    x[::97] = np.nan
+    x[5::131] = np.inf
+    x[7::211] = -np.inf
+    x[64:96] = 0.0
+    x[96:128] = -0.0
+    got = q4.quantize_q4_0(torch.from_numpy(x).cuda()).cpu().numpy()
+    assert np.array_equal(got, coracle.quantize_q4_0(x))
+
+
+def test_unpack_exact(q4, coracle):
+    n = 32 * 777 + 13
+    rng = np.random.default_rng(9)
+    w = (rng.standard_normal(n) * 0.3).astype(np.float16)
+    blocks = coracle.quantize_q4_0_f16(w)
+    got = q4.dequantize_q4_0(torch.from_numpy(blocks).cuda(), n).cpu().numpy()
+    assert np.array_equal(got, coracle.dequantize_q4_0(blocks, n))
+
+
+# ------------------------------------------------------------------ device form
+
+SHAPES = [(LAYOUT_KN, 32, 32), (LAYOUT_KN, 64, 96), (LAYOUT_KN, 160, 64), (LAYOUT_KN, 896, 2688),
+          (LAYOUT_KN, 3584, 896), (LAYOUT_NK, 32, 1), (LAYOUT_NK, 96, 37), (LAYOUT_NK, 224, 40),
+          (LAYOUT_NK, 896, 3584), (LAYOUT_NK, 896, 31500)]
+
+
+@pytest.mark.parametrize("layout,K,N", SHAPES)
+def test_repack_and_quantize_tiled(q4, coracle, layout, K, N):
+    rng = np.random.default_rng(K * 7 + N)
+    shape = (K, N) if layout == LAYOUT_KN else (N, K)
+    w = (rng.standard_normal(shape) * 0.02).astype(np.float16)
+    blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
+    expect = tiled_from_aos(blocks, layout, K, N)
+    wq = q4.Q4Weight.from_gguf_blocks(torch.from_numpy(blocks).cuda(), layout, K, N)
+    assert wq.buf.numel() == expect.size
+    eq, es = tiled_regions(expect, K, N)
+    gq, gs = tiled_regions(wq.buf.cpu().numpy(), K, N)
+    assert np.array_equal(gq, eq), "repack codes"
+    assert np.array_equal(gs, es), "repack scales"
+    wq2 = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
+    gq2, gs2 = tiled_regions(wq2.buf.cpu().numpy(), K, N)
+    assert np.array_equal(gq2, eq), "quantize_tiled codes"
+    assert np.array_equal(gs2, es), "quantize_tiled scales"
+
+
+# ------------------------------------------------------------------ projections
+
+def _run(q4, coracle, layout, K, N, M, out_dtype=torch.float32, bias=False, alpha=1.0, beta=0.0, seed=0,
+         wscale=0.02):
+    rng = np.random.default_rng(seed + 1000 * M + K + N)
+    shape = (K, N) if layout == LAYOUT_KN else (N, K)
+    w = (rng.standard_normal(shape) * wscale).astype(np.float16)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float16) if bias else None
+    blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
+    ref = coracle.matmul_ref(blocks, layout, K, N, x, b, alpha)
+    wq = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
+    # canaries: extra rows and columns around the output must stay untouched
+    ldy = N + 8
+    y0 = (rng.standard_normal((M + 2, ldy))).astype(np.float32)
+    yt = torch.from_numpy(y0).to(out_dtype).cuda()
+    view = yt[1:M + 1, :N]
+    from aria_b200._lib import call
+    from aria_b200.q4 import _stream
+    xt = torch.from_numpy(x).cuda()
+    bt = torch.from_numpy(b).cuda() if b is not None else None
+    call("aria_q4_0_matmul", wq.buf.data_ptr(), layout, K, N, xt.data_ptr(), M, K, view.data_ptr(),
+         0 if out_dtype == torch.float32 else 1, ldy, bt.data_ptr() if bt is not None else None,
+         float(alpha), float(beta), _stream())
+    out = yt.cpu().to(torch.float64).numpy()
+    y_init = torch.from_numpy(y0).to(out_dtype).to(torch.float64).numpy()
+    if beta != 0.0:
+        ref = ref + beta * y_init[1:M + 1, :N]
+    # canaries
+    assert np.array_equal(out[0], y_init[0]) and np.array_equal(out[M + 1], y_init[M + 1]), "row canary"
+    assert np.array_equal(out[1:M + 1, N:], y_init[1:M + 1, N:]), "column canary"
+    return out[1:M + 1, :N], ref
+
+
+def test_config0_single_projection(q4, coracle):
+    """ffn_up-shaped W[3584x896] NK, x[896] -> y[3584] fp32."""
+    y, ref = _run(q4, coracle, LAYOUT_NK, 896, 3584, 1)
+    check_close(y, ref, what="config0")
+
+
+EFKOLOS = [("qkv", LAYOUT_KN, 896, 2688), ("attn_out", LAYOUT_KN, 896, 896), ("ffn_up", LAYOUT_KN, 896, 3584),
+           ("ffn_down", LAYOUT_KN, 3584, 896), ("lm_head", LAYOUT_NK, 896, 31500)]
+
+
+@pytest.mark.parametrize("name,layout,K,N", EFKOLOS)
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 16])
+def test_efkolos_projections(q4, coracle, name, layout, K, N, M):
+    if name == "lm_head" and M > 4:
+        pytest.skip("fp64 oracle too slow for this size; covered at M<=4")
+    y, ref = _run(q4, coracle, layout, K, N, M, out_dtype=torch.float16, bias=True)
+    check_close(y, ref, what=f"{name} M={M}")
+
+
+@pytest.mark.parametrize("layout,K,N,M", [(LAYOUT_KN, 32, 32, 1), (LAYOUT_KN, 32, 32, 3), (LAYOUT_KN, 32, 32, 17),
+                                          (LAYOUT_NK, 32, 1, 1), (LAYOUT_NK, 64, 33, 17), (LAYOUT_NK, 1056, 5, 2),
+                                          (LAYOUT_KN, 4096, 64, 3), (LAYOUT_NK, 4096, 100, 1)])
+def test_odd_shapes(q4, coracle, layout, K, N, M):
+    y, ref = _run(q4, coracle, layout, K, N, M)
+    check_close(y, ref, what=f"odd {layout} {K}x{N} M={M}")
+
+
+def test_alpha_beta(q4, coracle):
+    y, ref = _run(q4, coracle, LAYOUT_KN, 896, 896, 2, alpha=0.5, beta=0.25)
+    check_close(y, ref, what="alpha/beta")
+    y, ref = _run(q4, coracle, LAYOUT_NK, 896, 640, 1, out_dtype=torch.float16, alpha=1 / 29.93, beta=1.0, bias=True)
+    check_close(y, ref, what="alpha/beta f16")
+
+
+def test_golden_projection_fixtures(q4, projection_fixtures):
+    for c in projection_fixtures:
+        K, N, M, layout = c["K"], c["N"], c["M"], c["layout"]
+        blocks = np.frombuffer(bytes.fromhex(c["blocks_hex"]), dtype=np.uint8).copy()
+        x = np.frombuffer(bytes.fromhex(c["x_f16_hex"]), dtype="<u2").view(np.float16).reshape(M, K).copy()
+        wq = q4.Q4Weight.from_gguf_blocks(torch.from_numpy(blocks).cuda(), layout, K, N)
+        y = q4.matmul(torch.from_numpy(x).cuda(), wq, out_dtype=torch.float32).cpu().numpy()
+        check_close(y, np.array(c["y_f64"]).reshape(M, N), what=f"golden {layout} {K}x{N}")
+
+
+def test_errors_are_raised(q4):
+    from aria_b200._lib import AriaQ4Error
+    w = q4.Q4Weight.from_f16(torch.zeros(64, 64, dtype=torch.float16, device="cuda"), LAYOUT_KN)
+    x = torch.zeros(1, 72, dtype=torch.float16, device="cuda")[:, 1:65]  # 2-byte offset: misaligned
+    with pytest.raises(AriaQ4Error) as ei:
+        q4.matmul(x, w)
+    assert ei.value.status == 3
+    with pytest.raises(AriaQ4Error) as ei:
+        q4.Q4Weight.from_f16(torch.zeros(64, 48, dtype=torch.float16, device="cuda"), LAYOUT_KN)
+    assert ei.value.status == 2
