@@ -21,7 +21,10 @@ int take_device_error();
 
 // M at or below which the register-fed decode kernel is used; above it the
 // tcgen05 kernel (each dequantised weight then serves up to 256 tokens).
-static const int kDecodeMaxM = 32;
+#ifndef ARIA_Q4_DECODE_MAX_M
+#define ARIA_Q4_DECODE_MAX_M 32
+#endif
+static const int kDecodeMaxM = ARIA_Q4_DECODE_MAX_M;
 
 using namespace aria_q4;
 

@@ -315,10 +315,12 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;
   a.y = y; a.ydt = ydt; a.ldy = ldy; a.bias = bias; a.alpha = alpha; a.beta = beta;
   if (layout == 1) {
+    if (M <= 32) return launch_tc_t<1, 32, 8>(a, x, ldx, st, pdl);
     if (M <= 64) return launch_tc_t<1, 64, 8>(a, x, ldx, st, pdl);
     if (M <= 128) return launch_tc_t<1, 128, 6>(a, x, ldx, st, pdl);
     return launch_tc_t<1, 256, 4>(a, x, ldx, st, pdl);
   }
+  if (M <= 32) return launch_tc_t<0, 32, 8>(a, x, ldx, st, pdl);
   if (M <= 64) return launch_tc_t<0, 64, 8>(a, x, ldx, st, pdl);
   if (M <= 128) return launch_tc_t<0, 128, 6>(a, x, ldx, st, pdl);
   return launch_tc_t<0, 256, 4>(a, x, ldx, st, pdl);
