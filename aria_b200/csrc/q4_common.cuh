@@ -19,7 +19,9 @@
 //                            that owns "t" therefore reads its 8-k slice of all
 //                            four 32-k blocks with one 16-byte load, and the
 //                            four lanes t = 0..3 of a row read 64 contiguous bytes.
-//      scales f16 NK: [N][Kp/32]   (one per (n, 32-k block): the block's own scale)
+//      scales f16 NK: [Kp/128][N][4]  (one per (n, 32-k block), group-major: the four
+//                                  block scales of a row's 128-k group are 8 contiguous
+//                                  bytes and consecutive rows are adjacent)
 //                 KN: [N/32][Kp]   (one per (k, 32-n block), transposed so that a
 //                                   32-row group reads its k scales contiguously)
 //    qs starts at byte 0, scales at align256(N*Kp/2).  Inside every 32-bit word

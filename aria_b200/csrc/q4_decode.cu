@@ -20,7 +20,8 @@
 // bottleneck, and staging dequantised weights through shared memory for
 // tcgen05 would cost 4 B of shared-memory traffic per weight.
 //
-// Scales: NK (blocks along k) -- one scale per (row, 32-k block); the block's two
+// Scales: NK (blocks along k) -- one scale per (row, 32-k block), stored
+// group-major so a row pair's four block scales are one 8-byte load; the block's two
 // MMAs accumulate from zero and are scaled in f32: exact products, f32 sums.
 // KN (blocks along n) -- one scale per (k, 32-row group); it is folded into the
 // activation fragment (x*s rounded to f16, relative error <= 2^-11).
@@ -116,7 +117,6 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
 #pragma unroll
     for (int e = 0; e < 4; e++) acc[j][e] = 0.0f;
 
-  const int KB = a.Kp >> 5;  // scale blocks per row (NK)
   const int grp = r0 >> 5;   // 32-row scale group (KN)
 
   if (active_warp) {
@@ -133,8 +133,8 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
           R[u].sa = make_uint2(0, 0);
           R[u].sb = make_uint2(0, 0);
           if (LAYOUT == 1) {
-            if (oka) R[u].sa = __ldg(reinterpret_cast<const uint2*>(a.scales + (size_t)ra * KB + 4 * G));
-            if (okb) R[u].sb = __ldg(reinterpret_cast<const uint2*>(a.scales + (size_t)rb * KB + 4 * G));
+            if (oka) R[u].sa = __ldg(reinterpret_cast<const uint2*>(a.scales + ((size_t)G * a.N + ra) * 4));
+            if (okb) R[u].sb = __ldg(reinterpret_cast<const uint2*>(a.scales + ((size_t)G * a.N + rb) * 4));
           }
         }
       }

@@ -6,19 +6,28 @@
 // :1583, :1686, :1753, :1805, :1864), which there runs with M = t tokens
 // (forward_gpu recomputes the whole prompt every step).
 //
-// One CTA computes D[128 weight rows][BT tokens] = W_tile[128 x K] . X_tile[BT x K]^T
-// ("swap AB": the weights are the 128-row UMMA operand, so each dequantised weight
-// serves BT = up to 256 tokens):
-//   warp 4      TMA producer: X tiles [BT x 64 k] f16, 128-byte swizzle, no multicast
-//   warps 0-3   dequantisers: one weight row per thread; the row's 128-k group of
-//               codes (64 B) is read straight from global memory into registers,
-//               turned into (q-8)*scale f16 (LOP3/HSUB/HMUL), and written as 16-byte
-//               chunks into the 128-byte-swizzled K-major A tile; then the epilogue
-//   warp 5      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BT, K=16,
-//               f16 x f16 -> f32 accumulator in TMEM), tcgen05.commit to release stages
-// Stages are mbarrier-ring buffered (STAGES deep).  Every wait is bounded (one
-// second); on expiry the kernel records an error code in g_device_error, unwinds,
-// frees its TMEM and returns instead of hanging the GPU.
+// Persistent kernel: one CTA per SM walks the output tiles D[128 weight rows][BT
+// tokens] = W_tile[128 x K] . X_tile[BT x K]^T ("swap AB": the weights are the
+// 128-row UMMA operand, so each dequantised weight serves BT = up to 256 tokens).
+// Fourteen warps, specialised:
+//   warp 8      TMA producer: X tiles [BT x 64 k] f16, 128-byte swizzle, no multicast
+//   warps 0-7   dequantisers, two warpgroups taking alternate 128-k groups (two 64-k
+//               stages each): one weight row per thread; the row's codes are streamed
+//               with cp.async into a shared-memory ring several groups ahead, turned into (q-8)*scale f16
+//               (LOP3/HSUB/HMUL) and written with tcgen05.st straight into tensor
+//               memory, where the MMA reads its A operand: the dequantised weights
+//               never cost shared-memory bandwidth (which X tiles alone keep near
+//               its 128 B/clk limit)
+//   warp 9      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BT, K=16,
+//               A from TMEM, B = X tile from shared memory, f32 accumulator in TMEM);
+//               tcgen05.commit releases operand stages and
+//               hands finished accumulators to the epilogue
+//   warps 10-13 epilogue: tcgen05.ld of one of two TMEM accumulators (so the next
+//               tile's MMAs overlap this tile's stores), alpha/bias/beta, f16/f32 store
+// Operand stages are an mbarrier ring (STAGES deep); the two accumulators have
+// their own full/empty barriers.  Every wait is bounded (one second); on expiry
+// the kernel records an error code in g_device_error, unwinds, frees its TMEM
+// and returns instead of hanging the GPU.
 //
 // The dequantised weight is rounded once to f16 ((q-8)*scale, relative error
 // <= 2^-11 per weight); products and sums are f32 in the tensor core.
@@ -39,218 +48,345 @@ struct TcArgs {
   float alpha, beta;
 };
 
-constexpr int kTcThreads = 192;
-constexpr int kBK = 64;                   // k per pipeline stage (one 128-byte swizzle row of f16)
-constexpr int kATileBytes = 128 * kBK * 2;  // 16 KB
+constexpr int kTcThreads = 448;  // 8 dequant + TMA + MMA + 4 epilogue warps
+constexpr int kBK = 64;        // k per pipeline stage (one 128-byte swizzle row of f16)
+constexpr int kAStageCols = 32;  // TMEM columns of one dequantised A stage: 128 rows x 64 k f16
+
+constexpr int kQDepth = 4;  // 128-k code groups in flight per dequant warpgroup
+// per warpgroup and ring slot: each row's whole 64-byte code group (128 rows) and
+// its scales (NK: 8 B per row; KN: 256 B per 32-row group)
+constexpr int kQSlot = 128 * 64;
+constexpr int kSSlot = 128 * 8 > 4 * 256 ? 128 * 8 : 4 * 256;
 
 template <int BT, int STAGES>
 struct TcSmem {
   static constexpr int kXTile = BT * kBK * 2;
-  static constexpr int kStage = kXTile + kATileBytes;
-  static constexpr int kBarOff = STAGES * kStage;
-  static constexpr int kBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
+  static constexpr int kStage = kXTile;
+  static constexpr int kQOff = STAGES * kStage;
+  static constexpr int kSOff = kQOff + 2 * kQDepth * kQSlot;
+  static constexpr int kBarOff = kSOff + 2 * kQDepth * kSSlot;
+  static constexpr int kBytes = kBarOff + 512 + 1024;  // barriers + alignment slack
 };
+
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tc::smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_8(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(tc::smem_u32(dst)), "l"(src), "r"(valid ? 8 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_4(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(tc::smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 template <int LAYOUT, int BT, int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const TcArgs a) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const TcArgs a, int n_tiles, int num_tiles) {
   using L = TcSmem<BT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // TMEM: two f32 accumulators [128 x BT] then kASlots dequantised A stages
+  constexpr int kASlots = (512 - 2 * BT) / kAStageCols >= 8 ? 8 : 4;  // two sub-rings of kASlots/2
+  constexpr int kAPer = kASlots / 2;
+  constexpr uint32_t kAColBase = 2 * BT;
+  constexpr uint32_t kNeed = 2 * BT + kASlots * kAStageCols;
+  constexpr uint32_t kCols = kNeed <= 32 ? 32 : kNeed <= 64 ? 64 : kNeed <= 128 ? 128 : kNeed <= 256 ? 256 : 512;
+  static_assert(kNeed <= 512, "TMEM budget");
+  // X tiles: one ring indexed by the CTA's stage counter (producer and MMA walk it
+  // in order).  Dequantised A stages: two private sub-rings of kASlots/2, one per
+  // dequant warpgroup, indexed by that warpgroup's own stage counter -- so no
+  // waiter can fall two phases behind a barrier whose slot another warpgroup uses.
   uint64_t* full_x = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* full_a = full_x + STAGES;
-  uint64_t* empty = full_a + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* empty_x = full_x + STAGES;
+  uint64_t* full_a = empty_x + STAGES;   // [kASlots]
+  uint64_t* empty_a = full_a + kASlots;  // [kASlots]
+  uint64_t* acc_full = empty_a + kASlots;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * 128;
-  const int m0 = blockIdx.y * BT;
   const int KT = (a.K + kBK - 1) / kBK;
-  constexpr uint32_t kCols = BT < 32 ? 32 : BT;
+  const int my_tiles = (num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       tc::mbar_init(&full_x[s], 1);
-      tc::mbar_init(&full_a[s], 128);
-      tc::mbar_init(&empty[s], 1);
+      tc::mbar_init(&empty_x[s], 1);
     }
-    tc::mbar_init(accum, 1);
+    for (int s = 0; s < kASlots; s++) {
+      tc::mbar_init(&full_a[s], 128);
+      tc::mbar_init(&empty_a[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      tc::mbar_init(&acc_full[b], 1);
+      tc::mbar_init(&acc_empty[b], 128);
+    }
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tmem_alloc(tmem_slot, kCols);
     tc::tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) tc::prefetch_tmap(&tmap_x);
+  if (warp == 8 && lane == 0) tc::prefetch_tmap(&tmap_x);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  const uint32_t tmem_d = *tmem_slot;
+  const uint32_t tmem_base = *tmem_slot;
 
   grid_dep_launch();
   grid_dep_wait();
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int issued = 0;
-      for (int it = 0; it < KT; it++) {
-        const int s = it % STAGES;
-        if (it >= STAGES && !tc::mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) {
-          tc::record_error(tc::kErrTimeoutEmpty);
-          break;
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < my_tiles && ok; j++) {
+        const int tile = blockIdx.x + j * gridDim.x;
+        const int m0 = (tile / n_tiles) * BT;
+        for (int kt = 0; kt < KT; kt++, it++) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !tc::mbar_wait(&empty_x[s], ((it / STAGES) - 1) & 1)) {
+            tc::record_error(tc::kErrTimeoutEmpty);
+            ok = false;
+            break;
+          }
+          tc::mbar_arrive_expect_tx(&full_x[s], L::kXTile);
+          tc::tma_load_2d(smem + s * L::kStage, &tmap_x, kt * kBK, m0, &full_x[s]);
         }
-        uint8_t* xs = smem + s * L::kStage;
-        tc::mbar_arrive_expect_tx(&full_x[s], L::kXTile);
-        tc::tma_load_2d(xs, &tmap_x, it * kBK, m0, &full_x[s]);
-        issued = it + 1;
       }
-      // drain: never leave the CTA while a copy into its shared memory is in flight
-      for (int it = (issued > STAGES ? issued - STAGES : 0); it < issued; it++)
-        tc::mbar_wait(&full_x[it % STAGES], (it / STAGES) & 1);
+      // never leave the CTA while a copy into its shared memory is in flight
+      for (int i = (it > STAGES ? it - STAGES : 0); i < it; i++)
+        tc::mbar_wait(&full_x[i % STAGES], (i / STAGES) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(128, BT);
+      int it = 0;
+      int acnt0 = 0, acnt1 = 0;  // stages consumed from each warpgroup's A sub-ring
       bool ok = true;
-      for (int it = 0; it < KT && ok; it++) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (!tc::mbar_wait(&full_x[s], ph) || !tc::mbar_wait(&full_a[s], ph)) {
-          tc::record_error(tc::kErrTimeoutFull);
+      for (int j = 0; j < my_tiles && ok; j++) {
+        const int buf = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
+          tc::record_error(tc::kErrTimeoutAccum);
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        const uint32_t xs = tc::smem_u32(smem + s * L::kStage);
-        const uint32_t as = xs + L::kXTile;
+        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT);
+        for (int kt = 0; kt < KT; kt++, it++) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          const int w = (kt >> 1) & 1;  // warpgroup that dequantised this stage
+          const int c = w ? acnt1++ : acnt0++;
+          const int as = w * kAPer + c % kAPer;
+          const uint32_t aph = (c / kAPer) & 1;
+          if (!tc::mbar_wait(&full_x[s], ph) || !tc::mbar_wait(&full_a[as], aph)) {
+            tc::record_error(tc::kErrTimeoutFull);
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t xs = tc::smem_u32(smem + s * L::kStage);
+          const uint32_t at = tmem_base + kAColBase + (uint32_t)(as * kAStageCols);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; kk++) {
-          const uint64_t adesc = tc::sdesc_k_sw128(as + kk * 32);
-          const uint64_t bdesc = tc::sdesc_k_sw128(xs + kk * 32);
-          tc::umma_f16(tmem_d, adesc, bdesc, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; kk++) {
+            const uint64_t bdesc = tc::sdesc_k_sw128(xs + kk * 32);
+            tc::umma_f16_ta(tmem_d, at + (uint32_t)(kk * 8), bdesc, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::umma_commit(&empty_x[s]);
+          tc::umma_commit(&empty_a[as]);
         }
-        tc::umma_commit(&empty[s]);
+        tc::umma_commit(&acc_full[buf]);  // also on the error path, so the epilogue is released
       }
       if (!ok) atomicExch(abort_flag, 1);
-      tc::umma_commit(accum);
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ dequantisers
-    const int r = threadIdx.x;  // 0..127: weight row n0 + r
-    const int n = n0 + r;
-    const bool row_ok = n < a.N;
+    // Two warpgroups: WG w (warps 4w..4w+3) owns the 128-k groups G = w, w+2, ...
+    // of every tile and feeds both of their 64-k stages.  Each thread owns one
+    // weight row (= TMEM lane) and streams the row's 64-byte code group plus its
+    // scales into a kQDepth-deep shared-memory ring with 16-byte cp.async, so
+    // loads run groups ahead without holding registers; the four 16-byte chunks
+    // of a row are stored XOR-swizzled by (row >> 1) & 3 so neighbouring rows'
+    // 128-bit reads hit distinct banks.  KN scales (one per k for a 32-row
+    // group) are shared by a warp: lanes 0..15 copy the group's 256 bytes.
+    const int wg = warp >> 2;         // 0 or 1
+    const int wl = warp & 3;          // warp within the warpgroup = TMEM lane quadrant
+    const int r = threadIdx.x & 127;  // weight row of the tile = TMEM lane
+    const int sw = (r >> 1) & 3;
     const size_t RB = (size_t)a.Kp >> 1;
-    const uint8_t* qrow = a.qs + (size_t)n * RB;
-    const int KB = a.Kp >> 5;
-    const int grp = n >> 5;
-    uint4 gq[4], gq_next[4];
-    uint2 gs = make_uint2(0, 0), gs_next = make_uint2(0, 0);
-    auto load_group = [&](int G, uint4 (&q)[4], uint2& sc) {
-      if (row_ok && G * 128 < a.Kp) {
+    const int KG = a.Kp >> 7;
+    const int gpt = (KG - wg + 1) / 2;  // groups of this warpgroup per tile
+    const int total = my_tiles * gpt;
+    uint8_t* qring = smem + L::kQOff + wg * kQDepth * kQSlot;
+    uint8_t* sring = smem + L::kSOff + wg * kQDepth * kSSlot;
+    auto issue = [&](int seq) {
+      const int slot = seq % kQDepth;
+      if (seq < total) {
+        const int j = seq / gpt, G = wg + 2 * (seq % gpt);
+        const int tile = blockIdx.x + j * gridDim.x;
+        const int nb = (tile % n_tiles) * 128;
+        const int n = nb + r;
+        const bool ok_row = n < a.N;
+        const size_t nn = ok_row ? (size_t)n : 0;
+        const uint8_t* src = a.qs + nn * RB + (size_t)G * 64;
+        uint8_t* dst = qring + slot * kQSlot + r * 64;
 #pragma unroll
-        for (int j = 0; j < 4; j++) q[j] = ld_stream_u4(qrow + (size_t)G * 64 + 16 * j);
-        if (LAYOUT == 1) sc = __ldg(reinterpret_cast<const uint2*>(a.scales + (size_t)n * KB + 4 * G));
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; j++) q[j] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-        sc = make_uint2(0, 0);
-      }
-    };
-    load_group(0, gq_next, gs_next);
-    bool ok = true;
-    for (int it = 0; it < KT; it++) {
-      const int s = it % STAGES;
-      const int G = it >> 1, h = it & 1;
-      if (h == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) gq[j] = gq_next[j];
-        gs = gs_next;
-        load_group(G + 1, gq_next, gs_next);  // one group ahead
-      }
-      if (it >= STAGES && !tc::mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) {
-        tc::record_error(tc::kErrTimeoutEmpty);
-        ok = false;
-        break;
-      }
-      uint8_t* arow = smem + s * L::kStage + L::kXTile + r * 128;
-      // words (t, i) with i in {2h, 2h+1}: local k = 32*(i-2h) + 8t, chunk c = 4*(i-2h) + t
-#pragma unroll
-      for (int t = 0; t < 4; t++) {
-        const uint4 q = gq[t];
-#pragma unroll
-        for (int ii = 0; ii < 2; ii++) {
-          const int i = 2 * h + ii;
-          const uint32_t w = (i == 0) ? q.x : (i == 1) ? q.y : (i == 2) ? q.z : q.w;
-          uint32_t d[4];
-          dequant_word_f16x2(w, d);
-          if (LAYOUT == 1) {
-            const uint32_t sw = (i < 2) ? gs.x : gs.y;
-            const uint32_t s1 = (i & 1) ? (sw >> 16) : (sw & 0xFFFFu);
-            const uint32_t s2 = s1 | (s1 << 16);
-#pragma unroll
-            for (int e = 0; e < 4; e++) d[e] = hmul2_u32(d[e], s2);
-          } else {
-            const int kk = G * 128 + 32 * i + 8 * t;
-            const uint4 s8 = row_ok ? __ldg(reinterpret_cast<const uint4*>(a.scales + (size_t)grp * a.Kp + kk))
-                                    : make_uint4(0, 0, 0, 0);
-            d[0] = hmul2_u32(d[0], s8.x);
-            d[1] = hmul2_u32(d[1], s8.y);
-            d[2] = hmul2_u32(d[2], s8.z);
-            d[3] = hmul2_u32(d[3], s8.w);
-          }
-          const int c = 4 * ii + t;
-          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = make_uint4(d[0], d[1], d[2], d[3]);
+        for (int q = 0; q < 4; q++) cp_async_16(dst + ((q ^ sw) << 4), src + 16 * q, ok_row);
+        if (LAYOUT == 1) {
+          cp_async_8(sring + slot * kSSlot + r * 8, a.scales + ((size_t)G * a.N + nn) * 4, ok_row);
+        } else if (lane < 16) {
+          const int grp = (nb + wl * 32) >> 5;
+          const bool ok_grp = grp * 32 < a.N;
+          const __half* ssrc = a.scales + (size_t)(ok_grp ? grp : 0) * a.Kp + (size_t)G * 128 + lane * 8;
+          cp_async_16(sring + slot * kSSlot + wl * 256 + lane * 16, ssrc, ok_grp);
         }
       }
-      tc::fence_proxy_async_smem();
-      tc::mbar_arrive(&full_a[s]);
+      cp_async_commit();  // an empty group keeps the wait count uniform
+    };
+#pragma unroll
+    for (int p = 0; p < kQDepth - 1; p++) issue(p);
+    bool ok = true;
+    int seq = 0;
+    int acnt = 0;  // stages this warpgroup has produced into its A sub-ring
+    for (int j = 0; j < my_tiles && ok; j++) {
+      for (int G = wg; G < KG && ok; G += 2, seq++) {
+        __syncwarp();  // every lane is done reading the slot the next issue overwrites
+        issue(seq + kQDepth - 1);
+        cp_async_wait<kQDepth - 1>();  // group `seq` has landed for this thread
+        __syncwarp();                  // ... and for the warp's shared KN scale row
+        const int slot = seq % kQDepth;
+        const uint8_t* qsrc = qring + slot * kQSlot + r * 64;
+        uint4 gq[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) gq[q] = *reinterpret_cast<const uint4*>(qsrc + ((q ^ sw) << 4));
+        const uint2 gs = (LAYOUT == 1) ? *reinterpret_cast<const uint2*>(sring + slot * kSSlot + r * 8)
+                                       : make_uint2(0, 0);
+        const uint8_t* kscale = sring + slot * kSSlot + wl * 256;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int kt = 2 * G + h;
+          if (kt >= KT) break;
+          const int c = acnt++;
+          const int s = wg * kAPer + c % kAPer;  // A slot in this warpgroup's sub-ring
+          if (c >= kAPer && !tc::mbar_wait(&empty_a[s], ((c / kAPer) - 1) & 1)) {
+            tc::record_error(tc::kErrTimeoutEmpty);
+            ok = false;
+            break;
+          }
+          // word (t, 2h+ii) holds local k = 32*ii + 8t .. +7, i.e. TMEM columns 16*ii + 4t .. +3
+          uint32_t av[32];
+#pragma unroll
+          for (int t = 0; t < 4; t++) {
+#pragma unroll
+            for (int ii = 0; ii < 2; ii++) {
+              const int i = 2 * h + ii;
+              const uint32_t w = (i == 0) ? gq[t].x : (i == 1) ? gq[t].y : (i == 2) ? gq[t].z : gq[t].w;
+              uint32_t d[4];
+              dequant_word_f16x2(w, d);
+              if (LAYOUT == 1) {
+                const uint32_t swd = (i < 2) ? gs.x : gs.y;
+                const uint32_t s1 = (i & 1) ? (swd >> 16) : (swd & 0xFFFFu);
+                const uint32_t s2 = s1 | (s1 << 16);
+#pragma unroll
+                for (int e = 0; e < 4; e++) d[e] = hmul2_u32(d[e], s2);
+              } else {
+                const uint4 s8 = *reinterpret_cast<const uint4*>(kscale + (32 * i + 8 * t) * 2);
+                d[0] = hmul2_u32(d[0], s8.x);
+                d[1] = hmul2_u32(d[1], s8.y);
+                d[2] = hmul2_u32(d[2], s8.z);
+                d[3] = hmul2_u32(d[3], s8.w);
+              }
+#pragma unroll
+              for (int e = 0; e < 4; e++) av[16 * ii + 4 * t + e] = d[e];
+            }
+          }
+          tc::tmem_st_32x32b_x32(tmem_base + ((uint32_t)(32 * wl) << 16) + kAColBase + (uint32_t)(s * kAStageCols),
+                                 av);
+          tc::tmem_st_wait();
+          tc::tc_fence_before();
+          tc::mbar_arrive(&full_a[s]);
+        }
+      }
     }
+    cp_async_wait<0>();  // no copy into shared memory may outlive the loop
     if (!ok) atomicExch(abort_flag, 1);
-
-    // ------------------------------------------------------------ epilogue
-    if (!tc::mbar_wait(accum, 0)) {
-      tc::record_error(tc::kErrTimeoutAccum);
-    } else if (*reinterpret_cast<volatile int*>(abort_flag) == 0) {
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 10..13)
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int rr = q * 32 + lane;
+    for (int j = 0; j < my_tiles; j++) {
+      const int buf = j & 1;
+      const int tile = blockIdx.x + j * gridDim.x;
+      const int n = (tile % n_tiles) * 128 + rr;
+      const int m0 = (tile / n_tiles) * BT;
+      if (!tc::mbar_wait(&acc_full[buf], (j >> 1) & 1)) {
+        tc::record_error(tc::kErrTimeoutAccum);
+        break;
+      }
+      if (*reinterpret_cast<volatile int*>(abort_flag) != 0) break;
       tc::tc_fence_after();
+      const bool row_ok = n < a.N;
       const float bias = (a.bias && row_ok) ? __half2float(a.bias[n]) : 0.0f;
+      const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT) + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
       for (int cc = 0; cc < BT / 32; cc++) {
         uint32_t v[32];
-        tc::tmem_ld_32x32b_x32(tmem_d + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cc * 32), v);
+        tc::tmem_ld_32x32b_x32(tmem_d + (uint32_t)(cc * 32), v);
         tc::tmem_ld_wait();
-        if (row_ok) {
+        const int tok0 = m0 + cc * 32;
+        if (!row_ok || tok0 >= a.M) continue;
+        const int ntok = min(32, a.M - tok0);
+        if (a.ydt == 1 && a.beta == 0.0f) {  // f16 out, no accumulate: the common path
+          __half* yp = reinterpret_cast<__half*>(a.y) + (size_t)tok0 * a.ldy + n;
+          if (ntok == 32) {
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int tok = m0 + cc * 32 + j;
-            if (tok < a.M) {
-              float o = a.alpha * __uint_as_float(v[j]) + bias;
-              const size_t idx = (size_t)tok * a.ldy + n;
-              if (a.ydt == 0) {
-                float* yp = reinterpret_cast<float*>(a.y) + idx;
-                if (a.beta != 0.0f) o += a.beta * *yp;
-                *yp = o;
-              } else {
-                __half* yp = reinterpret_cast<__half*>(a.y) + idx;
-                if (a.beta != 0.0f) o += a.beta * __half2float(*yp);
-                *yp = __float2half_rn(o);
-              }
+            for (int jj = 0; jj < 32; jj++) yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; jj++)
+              if (jj < ntok) yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 32; jj++) {
+            if (jj >= ntok) break;
+            float o = fmaf(a.alpha, __uint_as_float(v[jj]), bias);
+            const size_t idx = (size_t)(tok0 + jj) * a.ldy + n;
+            if (a.ydt == 0) {
+              float* yp = reinterpret_cast<float*>(a.y) + idx;
+              if (a.beta != 0.0f) o += a.beta * *yp;
+              *yp = o;
+            } else {
+              __half* yp = reinterpret_cast<__half*>(a.y) + idx;
+              if (a.beta != 0.0f) o += a.beta * __half2float(*yp);
+              *yp = __float2half_rn(o);
             }
           }
         }
       }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&acc_empty[buf]);
     }
   }
 
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem_d, kCols);
+    tc::tmem_dealloc(tmem_base, kCols);
   }
 }
 
@@ -293,8 +429,17 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
+  static int num_sms = 0;
+  if (num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (num_sms <= 0) num_sms = 148;
+  }
+  const int n_tiles = (a.N + 127) / 128;
+  const int num_tiles = n_tiles * ((a.M + BT - 1) / BT);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + 127) / 128, (a.M + BT - 1) / BT);
+  cfg.gridDim = dim3(num_tiles < num_sms ? num_tiles : num_sms);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = st;
@@ -303,7 +448,7 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, tm, a);
+  return cudaLaunchKernelEx(&cfg, kern, tm, a, n_tiles, num_tiles);
 }
 
 // Prefill-regime projection (M > 32).  BT (tokens per CTA) follows M.
@@ -314,16 +459,15 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
   a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;
   a.y = y; a.ydt = ydt; a.ldy = ldy; a.bias = bias; a.alpha = alpha; a.beta = beta;
+  // BT (tokens per tile) x STAGES under the TMEM budget 2*BT + 32*STAGES <= 512
   if (layout == 1) {
-    if (M <= 32) return launch_tc_t<1, 32, 8>(a, x, ldx, st, pdl);
     if (M <= 64) return launch_tc_t<1, 64, 8>(a, x, ldx, st, pdl);
-    if (M <= 128) return launch_tc_t<1, 128, 6>(a, x, ldx, st, pdl);
-    return launch_tc_t<1, 256, 4>(a, x, ldx, st, pdl);
+    if (M <= 128) return launch_tc_t<1, 128, 8>(a, x, ldx, st, pdl);
+    return launch_tc_t<1, 192, 4>(a, x, ldx, st, pdl);
   }
-  if (M <= 32) return launch_tc_t<0, 32, 8>(a, x, ldx, st, pdl);
   if (M <= 64) return launch_tc_t<0, 64, 8>(a, x, ldx, st, pdl);
-  if (M <= 128) return launch_tc_t<0, 128, 6>(a, x, ldx, st, pdl);
-  return launch_tc_t<0, 256, 4>(a, x, ldx, st, pdl);
+  if (M <= 128) return launch_tc_t<0, 128, 8>(a, x, ldx, st, pdl);
+  return launch_tc_t<0, 192, 4>(a, x, ldx, st, pdl);
 }
 
 // Reads and clears the device error flag (synchronous).

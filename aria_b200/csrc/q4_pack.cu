@@ -93,7 +93,7 @@ __global__ void repack_nk_scales_kernel(const uint8_t* __restrict__ blocks, int 
     const uint8_t* src = blocks + ((size_t)n * (K / kBlock) + b) * kBlockBytes;
     s = (uint16_t)(src[0] | (src[1] << 8));
   }
-  scales[id] = __ushort_as_half(s);
+  scales[((size_t)(b >> 2) * N + n) * 4 + (b & 3)] = __ushort_as_half(s);  // group-major [Kp/128][N][4]
 }
 
 // KN: block (k, g) covers n = 32g..32g+31 at row k.  A CTA takes the 128 k-rows
@@ -148,10 +148,11 @@ __global__ void quantize_tiled_nk_kernel(const T* __restrict__ w, int K, int N, 
   const int n = (int)(id / BPR), b = (int)(id % BPR);
   uint32_t* row = reinterpret_cast<uint32_t*>(qs + (size_t)n * qs_row_bytes(K));
   const int G = b >> 2, i = b & 3;
+  const size_t sidx = ((size_t)G * N + n) * 4 + i;  // group-major [Kp/128][N][4]
   if (b * kBlock >= K) {
 #pragma unroll
     for (int t = 0; t < 4; t++) row[16 * G + 4 * t + i] = 0x88888888u;
-    scales[id] = __ushort_as_half((uint16_t)0);
+    scales[sidx] = __ushort_as_half((uint16_t)0);
     return;
   }
   float v[kBlock];
@@ -162,7 +163,7 @@ __global__ void quantize_tiled_nk_kernel(const T* __restrict__ w, int K, int N, 
   const uint16_t s = quantize_block(v, kBlock, q);
 #pragma unroll
   for (int t = 0; t < 4; t++) row[16 * G + 4 * t + i] = dev_word_from_codes(q + 8 * t);
-  scales[id] = __ushort_as_half(s);
+  scales[sidx] = __ushort_as_half(s);
 }
 
 template <typename T>

@@ -19,7 +19,7 @@ def tiled_from_aos(blocks: np.ndarray, layout: int, K: int, N: int) -> np.ndarra
     qs: [N][Kp/2] bytes, row n = output feature n; word w of a row holds the 8
     consecutive k starting at 128*(w//16) + 32*(w%4) + 8*((w//4)%4), nibbles in
     the order e0 e2 e4 e6 e1 e3 e5 e7.  scales at align256(N*Kp/2):
-    NK -> [N][Kp/32], KN -> [N/32][Kp]."""
+    NK -> [Kp/128][N][4] (group-major), KN -> [N/32][Kp]."""
     Kp = (K + 127) // 128 * 128
     b = blocks.reshape(-1, 18)
     sc = b[:, 0:2].copy().view(np.uint16).reshape(-1)
@@ -31,8 +31,9 @@ def tiled_from_aos(blocks: np.ndarray, layout: int, K: int, N: int) -> np.ndarra
     qd = np.full((N, Kp), 8, dtype=np.uint32)
     if layout == LAYOUT_NK:
         qd[:, :K] = flat.reshape(N, K)
-        sdev = np.zeros((N, Kp // 32), dtype=np.uint16)
-        sdev[:, :K // 32] = sc.reshape(N, K // 32)
+        rows = np.zeros((N, Kp // 32), dtype=np.uint16)
+        rows[:, :K // 32] = sc.reshape(N, K // 32)
+        sdev = rows.reshape(N, Kp // 128, 4).transpose(1, 0, 2)  # group-major [Kp/128][N][4]
     else:
         qd[:, :K] = flat.reshape(K, N).T
         sdev = np.zeros((N // 32, Kp), dtype=np.uint16)

@@ -22,7 +22,7 @@ def _decode_tiled(buf, layout, K, N):
             q[:, k_of_word(w) + e] = (words[:, w] >> (4 * dev_pos(e))) & 0xF
     s = sc.view("<u2").view(np.float16).astype(np.float32)
     if layout == LAYOUT_NK:
-        s = np.repeat(s.reshape(N, Kp // 32), 32, axis=1)
+        s = np.repeat(s.reshape(Kp // 128, N, 4).transpose(1, 0, 2).reshape(N, Kp // 32), 32, axis=1)
     else:
         s = np.repeat(s.reshape(N // 32, Kp), 32, axis=0)
     return ((q - 8) * s)[:, :K]
