@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill", type=lambda v: [int(t) for t in v.split(",") if t], default=[4096, 8192])
+    ap.add_argument("--batched", type=lambda v: [int(t) for t in v.split(",") if t], default=[16, 64, 256])
     return ap.parse_args()
 
 
@@ -200,7 +202,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    def timed(fn, steps, warmup):
+    def timed(fn, steps, warmup, tag="aria_timed"):
         with torch.cuda.stream(stream):
             for i in range(warmup):
                 fn(i)
@@ -208,10 +210,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             barrier()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push(tag)  # lets an ncu launch list select exactly the timed work
             e0.record(stream)
             for i in range(steps):
                 fn(i)
             e1.record(stream)
+            torch.cuda.nvtx.range_pop()
             torch.cuda.synchronize()
             barrier()
         ms = e0.elapsed_time(e1)
@@ -221,10 +225,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             ms = float(t.item())
         return ms
 
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
     sampler = ClockSampler(local_rank)
     sampler.start()
-    ms = timed(lambda i: graphs[i % reps].replay(), args.steps, args.warmup)
-    clocks = sampler.stop()
+    ms = timed(lambda i: graphs[i % reps].replay(), args.steps, args.warmup, "aria_decode_step")
     ms_step = ms / args.steps
     bytes_step = prog.algorithmic_bytes()
     value = bytes_step * world / (ms_step * 1e-3) / 1e9
@@ -249,7 +258,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             with torch.cuda.graph(g, stream=stream):
                 for j in range(n_launch):
                     matmul(x_, pool[j % ncopy], y_)
-        kms = timed(lambda i: g.replay(), 3, 2) / (3 * n_launch)
+        kms = timed(lambda i: g.replay(), 3, 2, f"aria_kind_{kind}") / (3 * n_launch)
         abytes = w0.nbytes + w0.K * 2 + w0.N * 2
         per_kind[kind] = {"us_per_launch": round(kms * 1e3, 3), "launches_per_step": len(idxs),
                           "share_est": kms * len(idxs), "alg_bytes": abytes,
@@ -257,14 +266,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         del g, pool
         torch.cuda.empty_cache()
     dom = max(per_kind, key=lambda k: per_kind[k]["share_est"])
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except OSError:
-        pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    roof = {"bound": "hbm", "kernel": f"gemv_kernel ({dom})", "achieved": per_kind[dom]["gbs"], "peak": hbm_peak,
+    roof = {"bound": "hbm", "kernel": f"decode_mma_kernel ({dom})", "achieved": per_kind[dom]["gbs"], "peak": hbm_peak,
             "unit": "GB/s", "frac": per_kind[dom]["gbs"] / hbm_peak, "traffic": None,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
             "per_kind": per_kind}
@@ -279,8 +282,54 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         graphs[i % reps].replay()
         out_host.copy_(prog.ys[-1], non_blocking=True)
 
-    e2e_ms = timed(e2e_step, args.steps, args.warmup) / args.steps
+    e2e_ms = timed(e2e_step, args.steps, args.warmup, "aria_e2e") / args.steps
     e2e_val = bytes_step * world / (e2e_ms * 1e-3) / 1e9
+    del x_host, out_host
+
+    # ---- batched decode and prefill: same weights, larger M.
+    # Each projection reads its own activation buffer, so a prefill step's inputs
+    # (>= 1 GB at M=4096) are never L2-resident; batched decode rotates replicas.
+    flops_token = cfg.flops_per_token()
+    bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
+    bf16_sus = float(peaks.get("bf16_tflops_sustained", 1420.0))
+    batched = {}
+    for M in args.batched:
+        bprog = DecodeProgram(stack0, M=M, seed=rank + 11)
+        bgraphs = []
+        with torch.cuda.stream(stream):
+            for st in stacks:
+                bprog.run(st)
+            torch.cuda.synchronize()
+            for st in stacks:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    bprog.run(st)
+                bgraphs.append(g)
+        bsteps = max(5, args.steps // 4)
+        bms = timed(lambda i: bgraphs[i % reps].replay(), bsteps, max(3, args.warmup // 4), f"aria_batched_M{M}") / bsteps
+        batched[f"M{M}"] = {"ms_per_step": bms, "GBs": bprog.algorithmic_bytes() * world / (bms * 1e-3) / 1e9,
+                            "TFLOPs": M * flops_token * world / (bms * 1e-3) / 1e12,
+                            "tokens_per_s": M * world / (bms * 1e-3)}
+        del bgraphs, bprog
+        torch.cuda.empty_cache()
+    prefill = {}
+    for M in args.prefill:
+        pprog = DecodeProgram(stack0, M=M, seed=rank + 21)
+        with torch.cuda.stream(stream):
+            pprog.run()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                pprog.run()
+        psteps = max(3, args.steps // 20)
+        pms = timed(lambda i: g.replay(), psteps, 3, f"aria_prefill_M{M}") / psteps
+        tf = M * flops_token * world / (pms * 1e-3) / 1e12
+        prefill[f"M{M}"] = {"ms_per_step": pms, "tokens_per_s": M * world / (pms * 1e-3), "TFLOPs": tf,
+                            "frac_of_measured_bf16_peak": tf / world / bf16_peak,
+                            "frac_of_measured_sustained_peak": tf / world / bf16_sus}
+        del g, pprog
+        torch.cuda.empty_cache()
+    clocks = sampler.stop()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -295,6 +344,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                       "l2_policy": f"rotate {reps} weight replicas ({reps * stack0.nbytes / 2**20:.0f} MiB > 4x L2)",
                       "parallelism": f"batch-sharded replicas x{world}"},
            "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+           "batched_decode": {"workload": "BASELINE configs[2]: same 101 projections, M tokens per step",
+                              **batched},
+           "prefill": {"workload": "BASELINE configs[3]: 101 projections of the 20 layers + LM head over M "
+                                   "tokens (8x512 = 4096, 4x2048 = 8192), tcgen05 kernel",
+                       "flops_per_token": flops_token, "peak_tflops_measured": bf16_peak,
+                       "peak_tflops_sustained": bf16_sus, **prefill},
            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": prog.input_bytes(),
                    "d2h_bytes_per_step": prog.ys[-1].numel() * 2, "ms_per_step": e2e_ms},
            "gpu_launches": prog.launches * args.steps}
