@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Workload: one Efkolos decode step at batch 1 -- the
-101 Q4_0 projections of a token (20 layers x QKV 896->2688, attn_out 896->896,
+81 Q4_0 projections of a token (20 layers x QKV 896->2688, attn_out 896->896,
 ffn_up 896->3584, ffn_down 3584->896, plus the LM head 896->31500), launched in
 model order through the C ABI, each waiting on the previous (programmatic
 dependent launch), captured once in a CUDA graph per weight replica.  Metric:
@@ -344,9 +344,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                       "l2_policy": f"rotate {reps} weight replicas ({reps * stack0.nbytes / 2**20:.0f} MiB > 4x L2)",
                       "parallelism": f"batch-sharded replicas x{world}"},
            "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
-           "batched_decode": {"workload": "BASELINE configs[2]: same 101 projections, M tokens per step",
+           "batched_decode": {"workload": "BASELINE configs[2]: same 81 projections, M tokens per step",
                               **batched},
-           "prefill": {"workload": "BASELINE configs[3]: 101 projections of the 20 layers + LM head over M "
+           "prefill": {"workload": "BASELINE configs[3]: 81 projections of the 20 layers + LM head over M "
                                    "tokens (8x512 = 4096, 4x2048 = 8192), tcgen05 kernel",
                        "flops_per_token": flops_token, "peak_tflops_measured": bf16_peak,
                        "peak_tflops_sustained": bf16_sus, **prefill},
