@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(_PKG, "libaria_q4.so")
 # status codes (aria_q4_status)
 OK, EINVAL, EUNSUPPORTED, EALIGN, ECUDA, ENODEVICE, ESIZE = range(7)
 LAYOUT_KN, LAYOUT_NK = 0, 1
+FLAG_CONST_WEIGHTS = 1
 F32, F16 = 0, 1
 
 # every symbol include/aria_q4.h declares: (restype, argtypes)
@@ -32,6 +33,7 @@ SIGNATURES = {
     "aria_q4_0_repack": (_I, [_P, _I, _I, _I, _P, _SZ, _P]),
     "aria_q4_0_quantize_tiled": (_I, [_P, _I, _I, _I, _P, _SZ, _P]),
     "aria_q4_0_matmul": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _F, _F, _P]),
+    "aria_q4_0_matmul_ex": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _F, _F, _I, _P]),
     "aria_q4_strerror": (ctypes.c_char_p, [_I]),
     "aria_q4_last_cuda_error": (_I, []),
     "aria_q4_take_device_error": (_I, []),

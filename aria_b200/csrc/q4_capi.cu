@@ -13,7 +13,8 @@ cudaError_t launch_unpack(const uint8_t* blocks, size_t n, float* dst, cudaStrea
 cudaError_t launch_repack(const uint8_t* blocks, int layout, int K, int N, uint8_t* tiled, cudaStream_t st);
 cudaError_t launch_quantize_tiled(const uint16_t* w, int layout, int K, int N, uint8_t* tiled, cudaStream_t st);
 cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
-                          int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl);
+                          int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
+                          bool const_weights);
 cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                            int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl);
 int take_device_error();
@@ -22,7 +23,7 @@ int take_device_error();
 // M at or below which the register-fed decode kernel is used; above it the
 // tcgen05 kernel (each dequantised weight then serves up to 256 tokens).
 #ifndef ARIA_Q4_DECODE_MAX_M
-#define ARIA_Q4_DECODE_MAX_M 32
+#define ARIA_Q4_DECODE_MAX_M 64
 #endif
 static const int kDecodeMaxM = ARIA_Q4_DECODE_MAX_M;
 
@@ -111,22 +112,33 @@ int aria_q4_0_quantize_tiled(const uint16_t* w, int layout, int K, int N, void* 
   return cuda_status(launch_quantize_tiled(w, layout, K, N, (uint8_t*)tiled, (cudaStream_t)stream));
 }
 
-int aria_q4_0_matmul(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
-                     int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, void* stream) {
+int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
+                        int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, int flags, void* stream) {
   if (int s = check_tiled_shape(layout, K, N)) return s;
   if (M < 0) return ARIA_Q4_EINVAL;
   if (M == 0) return ARIA_Q4_OK;
   if (!tiled || !x || !y) return ARIA_Q4_EINVAL;
   if (y_dtype != ARIA_Q4_F16 && y_dtype != ARIA_Q4_F32) return ARIA_Q4_EINVAL;
   if (ldx < K || ldy < N) return ARIA_Q4_EINVAL;
+  if ((flags & ~ARIA_Q4_FLAG_CONST_WEIGHTS) != 0) return ARIA_Q4_EINVAL;
   if (((uintptr_t)tiled & 255u) != 0 || !aligned16(x) || (ldx % 8) != 0) return ARIA_Q4_EALIGN;
   if (int s = check_device()) return s;
   const cudaStream_t st = (cudaStream_t)stream;
-  if (M <= kDecodeMaxM)
+  // Kernel choice: the register-fed decode kernel up to 32 tokens (and up to 64
+  // when the output has too few 128-row tiles to fill the GPU with tcgen05 work);
+  // the tcgen05 kernel above that.
+  const bool decode = M <= 32 || (M <= kDecodeMaxM && N < 8192);
+  if (decode)
     return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
-                                     (const __half*)bias, alpha, beta, st, true));
+                                     (const __half*)bias, alpha, beta, st, true,
+                                     (flags & ARIA_Q4_FLAG_CONST_WEIGHTS) != 0));
   return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
                                     (const __half*)bias, alpha, beta, st, true));
+}
+
+int aria_q4_0_matmul(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
+                     int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, void* stream) {
+  return aria_q4_0_matmul_ex(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, 0, stream);
 }
 
 const char* aria_q4_strerror(int status) {

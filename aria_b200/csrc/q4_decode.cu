@@ -1,9 +1,9 @@
-// q4_decode.cu -- decode / skinny regime Q4_0 projection (M <= 32 token rows).
+// q4_decode.cu -- decode / skinny regime Q4_0 projection (M <= 64 token rows).
 //
 // Replaces, for Q4_0 weights, the cuBLAS fp16 GEMM that ARIA runs for every
 // projection (`gemm()` at lold3344/ARIA src/transformer_cuda.rs:615-640, called
 // at :1583 QKV, :1686 attn_out, :1753 ffn_up, :1805 ffn_down, :1864 LM head).
-// At M <= 32 that product is bound by weight bytes: this kernel streams 0.5625 B
+// At small M that product is bound by weight bytes: this kernel streams 0.5625 B
 // per weight (the Q4_0 codes and scales) instead of the 2 B of f16 weights.
 //
 // Design (B200): the weights never touch shared memory.  A warp owns a tile of
@@ -26,10 +26,14 @@
 // KN (blocks along n) -- one scale per (k, 32-row group); it is folded into the
 // activation fragment (x*s rounded to f16, relative error <= 2^-11).
 //
-// K is split across the warps of a CTA (up to 8); partial fragments are reduced
-// in shared memory.  No global scratch.  Launch uses programmatic dependent
+// K is split across the warps of a CTA (up to 8) and, for tall-K shapes with few
+// tiles, across a thread-block cluster of up to 4 CTAs; partial fragments are
+// reduced in shared memory and then through distributed shared memory.  No
+// global scratch.  Launch uses programmatic dependent
 // launch: before griddepcontrol.wait a CTA only prefetches its weight rows to
-// L2, so weight streaming overlaps the previous kernel's tail.
+// L2 -- or, when the caller declares the weights constant (not written by the
+// preceding kernel), loads its first batch of codes and scales into registers
+// -- so weight streaming overlaps the previous kernel's tail.
 #include "q4_common.cuh"
 
 namespace aria_q4 {
@@ -44,7 +48,9 @@ struct DecodeArgs {
   int ydt, ldy;
   const __half* bias;
   float alpha, beta;
-  int ksplit;  // warps per 16-row tile
+  int ksplit;  // warps per 16-row tile (within a CTA)
+  int csplit;  // CTAs per tile group (a thread-block cluster along x)
+  int const_weights;  // weights are not written by the preceding kernel: load them before the dependency wait
 };
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t a0, const uint32_t a1, const uint32_t a2,
@@ -75,26 +81,46 @@ __device__ __forceinline__ uint4 ld_u4_or(const void* p, bool ok, uint32_t fill)
   return ok ? ld_weights_u4(p) : make_uint4(fill, fill, fill, fill);
 }
 
-// One 128-k group of a 16-row tile for one warp: 2 rows x 16 bytes per lane.
+// One 128-k group of a 16-row tile for one warp: two rows' codes (16 B per lane),
+// NK block scales, and -- when the batch preloads them -- the activation and KN
+// scale fragments of the group's four 32-k blocks.
+template <int NT, bool PRE>
 struct GroupRegs {
   uint4 qa, qb;
   uint2 sa, sb;
+  uint4 xv[PRE ? 4 : 1][PRE ? NT : 1];
+  uint4 ks[PRE ? 4 : 1];
 };
 
-template <int LAYOUT, int NT, int MAXB>
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(const float* local_addr, uint32_t rank) {
+  uint32_t remote, v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(tc_smem_u32(local_addr)), "r"(rank));
+  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+  return __uint_as_float(v);
+}
+
+// PRE: the batch phase also loads every activation / KN-scale fragment of its
+// groups (small NT), so no load latency is exposed inside the MMA loop.
+template <int LAYOUT, int NT, int MAXB, bool PRE>
 __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) {
   __shared__ float red[8][32][NT * 4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int S = a.ksplit;
+  const int S = a.ksplit, C = a.csplit;
   const int tiles_per_cta = 8 / S;
   const int slot = warp / S, ks = warp % S;
   const bool active_warp = slot < tiles_per_cta;
-  const int tile = blockIdx.x * tiles_per_cta + slot;
+  const int crank = (int)blockIdx.x % C;  // rank in the cluster (clusters run along x)
+  const int tile = ((int)blockIdx.x / C) * tiles_per_cta + slot;
   const int r0 = tile * 16;
   const int KG = a.Kp >> 7;
-  const int gps = (KG + S - 1) / S;
-  const int gbeg = ks * gps, gend = min(KG, gbeg + gps);
+  const int nslices = S * C;
+  const int gps = (KG + nslices - 1) / nslices;
+  const int gbeg = (crank * S + ks) * gps, gend = min(KG, gbeg + gps);
   const size_t RB = (size_t)a.Kp >> 1;
   const int m0 = blockIdx.y * 8 * NT;
 
@@ -103,60 +129,93 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
   const uint8_t* qa_ptr = a.qs + (size_t)ra * RB + 16 * t;
   const uint8_t* qb_ptr = a.qs + (size_t)rb * RB + 16 * t;
 
-  // weights are load-time constants: start streaming them towards L2 now
-  if (active_warp && t == 0 && gend > gbeg) {
-    if (oka) bulk_prefetch_l2(a.qs + (size_t)ra * RB + (size_t)gbeg * 64, (uint32_t)(gend - gbeg) * 64u);
-    if (okb) bulk_prefetch_l2(a.qs + (size_t)rb * RB + (size_t)gbeg * 64, (uint32_t)(gend - gbeg) * 64u);
-  }
-  grid_dep_launch();
-  grid_dep_wait();
-
   float acc[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; j++)
 #pragma unroll
     for (int e = 0; e < 4; e++) acc[j][e] = 0.0f;
 
-  const int grp = r0 >> 5;   // 32-row scale group (KN)
+  const int grp = r0 >> 5;  // 32-row scale group (KN)
+  auto load_x = [&](int kb, int j) -> uint4 {
+    const int tok = m0 + 8 * j + g;
+    return (tok < a.M && kb < a.K) ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)tok * a.ldx + kb + 8 * t))
+                                   : make_uint4(0, 0, 0, 0);
+  };
+  auto load_ks = [&](int kb) -> uint4 {
+    return (active_warp && kb < a.Kp) ? __ldg(reinterpret_cast<const uint4*>(a.scales + (size_t)grp * a.Kp + kb + 8 * t))
+                                      : make_uint4(0, 0, 0, 0);
+  };
+  GroupRegs<NT, PRE> R[MAXB];
+  // codes and scales of one batch of groups (load-time constants)
+  auto load_weights = [&](int gb, int nb) {
+#pragma unroll
+    for (int u = 0; u < MAXB; u++) {
+      if (u < nb) {
+        const int G = gb + u;
+        R[u].qa = ld_u4_or(qa_ptr + (size_t)G * 64, oka, 0x88888888u);
+        R[u].qb = ld_u4_or(qb_ptr + (size_t)G * 64, okb, 0x88888888u);
+        R[u].sa = make_uint2(0, 0);
+        R[u].sb = make_uint2(0, 0);
+        if (LAYOUT == 1) {
+          if (oka) R[u].sa = __ldg(reinterpret_cast<const uint2*>(a.scales + ((size_t)G * a.N + ra) * 4));
+          if (okb) R[u].sb = __ldg(reinterpret_cast<const uint2*>(a.scales + ((size_t)G * a.N + rb) * 4));
+        }
+        if (PRE && LAYOUT == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) R[u].ks[i] = load_ks(G * 128 + i * 32);
+        }
+      }
+    }
+  };
+  // activations of one batch (written by the preceding kernel: only after the wait)
+  auto load_acts = [&](int gb, int nb) {
+    if (PRE) {
+#pragma unroll
+      for (int u = 0; u < MAXB; u++)
+        if (u < nb)
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < NT; j++) R[u].xv[i][j] = load_x((gb + u) * 128 + i * 32, j);
+    }
+  };
+
+  const bool early = a.const_weights != 0 && active_warp && gend > gbeg;
+  if (early) {
+    load_weights(gbeg, min(MAXB, gend - gbeg));  // overlaps the previous kernel's tail
+  } else if (active_warp && t == 0 && gend > gbeg) {
+    // weights may have been written by the previous kernel: only warm L2 before the wait
+    if (oka) bulk_prefetch_l2(a.qs + (size_t)ra * RB + (size_t)gbeg * 64, (uint32_t)(gend - gbeg) * 64u);
+    if (okb) bulk_prefetch_l2(a.qs + (size_t)rb * RB + (size_t)gbeg * 64, (uint32_t)(gend - gbeg) * 64u);
+  }
+  grid_dep_launch();
+  grid_dep_wait();
 
   if (active_warp) {
     for (int gb = gbeg; gb < gend; gb += MAXB) {
       const int nb = min(MAXB, gend - gb);
-      // issue every load of this batch before any arithmetic (up to MAXB KB in flight per warp)
-      GroupRegs R[MAXB];
-#pragma unroll
-      for (int u = 0; u < MAXB; u++) {
-        if (u < nb) {
-          const int G = gb + u;
-          R[u].qa = ld_u4_or(qa_ptr + (size_t)G * 64, oka, 0x88888888u);
-          R[u].qb = ld_u4_or(qb_ptr + (size_t)G * 64, okb, 0x88888888u);
-          R[u].sa = make_uint2(0, 0);
-          R[u].sb = make_uint2(0, 0);
-          if (LAYOUT == 1) {
-            if (oka) R[u].sa = __ldg(reinterpret_cast<const uint2*>(a.scales + ((size_t)G * a.N + ra) * 4));
-            if (okb) R[u].sb = __ldg(reinterpret_cast<const uint2*>(a.scales + ((size_t)G * a.N + rb) * 4));
-          }
-        }
-      }
+      if (!(early && gb == gbeg)) load_weights(gb, nb);
+      load_acts(gb, nb);
 #pragma unroll
       for (int u = 0; u < MAXB; u++) {
         if (u >= nb) break;
         const int G = gb + u;
         const uint32_t qaw[4] = {R[u].qa.x, R[u].qa.y, R[u].qa.z, R[u].qa.w};
         const uint32_t qbw[4] = {R[u].qb.x, R[u].qb.y, R[u].qb.z, R[u].qb.w};
+        uint4 ksg[4];
+        if (!PRE && LAYOUT == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) ksg[i] = load_ks(G * 128 + i * 32);  // the group's KN scales at once
+        }
 #pragma unroll
         for (int i = 0; i < 4; i++) {
           const int kb = G * 128 + i * 32;
           if (kb >= a.K) break;  // padded tail of K (uniform across the warp)
           uint4 xv[NT];
 #pragma unroll
-          for (int j = 0; j < NT; j++) {
-            const int tok = m0 + 8 * j + g;
-            xv[j] = (tok < a.M) ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)tok * a.ldx + kb + 8 * t))
-                                : make_uint4(0, 0, 0, 0);
-          }
+          for (int j = 0; j < NT; j++) xv[j] = PRE ? R[u].xv[PRE ? i : 0][PRE ? j : 0] : load_x(kb, j);
           if (LAYOUT == 0) {
-            const uint4 s8 = __ldg(reinterpret_cast<const uint4*>(a.scales + (size_t)grp * a.Kp + kb + 8 * t));
+            const uint4 s8 = PRE ? R[u].ks[PRE ? i : 0] : ksg[i];
 #pragma unroll
             for (int j = 0; j < NT; j++) {
               xv[j].x = hmul2_u32(xv[j].x, s8.x);
@@ -191,20 +250,43 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
     }
   }
 
-  if (S > 1) {
+  // Reduction over the K slices: the S warps of a tile in shared memory, then
+  // (C > 1) the C CTAs of the cluster through distributed shared memory into
+  // cluster rank 0.  Every thread reaches every barrier: no early return above.
+  const bool leader = active_warp && ks == 0;
+  if (S > 1 || C > 1) {
 #pragma unroll
     for (int j = 0; j < NT; j++)
 #pragma unroll
       for (int e = 0; e < 4; e++) red[warp][lane][j * 4 + e] = acc[j][e];
     __syncthreads();
-    if (ks != 0 || !active_warp) return;
-    for (int s = 1; s < S; s++)
+    if (leader) {
+      for (int s2 = 1; s2 < S; s2++)
 #pragma unroll
-      for (int j = 0; j < NT; j++)
+        for (int j = 0; j < NT; j++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) acc[j][e] += red[warp + s][lane][j * 4 + e];
+          for (int e = 0; e < 4; e++) acc[j][e] += red[warp + s2][lane][j * 4 + e];
+    }
+    if (C > 1) {
+      __syncthreads();  // the leader rows of red are rewritten below
+      if (leader) {
+#pragma unroll
+        for (int j = 0; j < NT; j++)
+#pragma unroll
+          for (int e = 0; e < 4; e++) red[warp][lane][j * 4 + e] = acc[j][e];
+      }
+      cluster_sync_all();  // every CTA's partial is in its shared memory
+      if (leader && crank == 0) {
+        for (int rr = 1; rr < C; rr++)
+#pragma unroll
+          for (int j = 0; j < NT; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[j][e] += ld_dsmem_f32(&red[warp][lane][j * 4 + e], (uint32_t)rr);
+      }
+      cluster_sync_all();  // peers keep their shared memory until rank 0 has read it
+    }
   }
-  if (!active_warp) return;
+  if (!leader || crank != 0) return;
 
   // D fragment: c0,c1 -> (row g, tokens 2t, 2t+1); c2,c3 -> (row g+8, same tokens)
   float bia = 0.f, bib = 0.f;
@@ -227,38 +309,55 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
   }
 }
 
-template <int LAYOUT, int NT, int MAXB>
+template <int LAYOUT, int NT, int MAXB, bool PRE>
 static cudaError_t launch_t(const DecodeArgs& a, cudaStream_t st, bool pdl) {
   const int tiles = (a.N + 15) / 16;
   const int tpc = 8 / a.ksplit;
-  dim3 grid((tiles + tpc - 1) / tpc, (a.M + 8 * NT - 1) / (8 * NT));
+  dim3 grid(((tiles + tpc - 1) / tpc) * a.csplit, (a.M + 8 * NT - 1) / (8 * NT));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+  }
+  if (a.csplit > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = a.csplit;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<LAYOUT, NT, MAXB>, a);
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<LAYOUT, NT, MAXB, PRE>, a);
 }
 
-template <int LAYOUT, int NT>
-static cudaError_t launch_nt(const DecodeArgs& a, int maxb, cudaStream_t st, bool pdl) {
-  if (maxb <= 1) return launch_t<LAYOUT, NT, 1>(a, st, pdl);
-  if (maxb <= 2) return launch_t<LAYOUT, NT, 2>(a, st, pdl);
-  return launch_t<LAYOUT, NT, 4>(a, st, pdl);
+template <int LAYOUT>
+static cudaError_t launch_layout(const DecodeArgs& a, int nt, int gpw, cudaStream_t st, bool pdl) {
+  // register budget (128/thread at 2 CTAs per SM): preloading the activation
+  // fragments is affordable for one or two token tiles
+  if (nt == 1) return gpw <= 1 ? launch_t<LAYOUT, 1, 1, true>(a, st, pdl) : launch_t<LAYOUT, 1, 2, true>(a, st, pdl);
+  if (nt == 2) return launch_t<LAYOUT, 2, 1, true>(a, st, pdl);
+  if (nt == 4) return launch_t<LAYOUT, 4, 1, false>(a, st, pdl);
+  return launch_t<LAYOUT, 8, 1, false>(a, st, pdl);
 }
 
-// Decode-regime projection for M <= 32 (larger M goes to the tcgen05 kernel).
-// Work split: a 16-row tile's K is cut into `ksplit` slices (one warp each) only
-// when there are too few tiles to give every SM eight warps; a warp then loads
-// its whole slice (up to 8 groups = 8 KB per warp) before computing.
+// Decode-regime projection for M <= 64 (larger M goes to the tcgen05 kernel).
+// Work split: a 16-row tile's K is cut into `ksplit` slices (one warp each) when
+// there are too few tiles to give every SM sixteen warps; if that still leaves
+// SMs idle and K is long, a cluster of `csplit` CTAs splits K further and
+// reduces through distributed shared memory.
 cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
-                          int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl) {
+                          int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
+                          bool const_weights) {
   DecodeArgs a;
+  a.const_weights = const_weights ? 1 : 0;
   a.qs = tiled;
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
   a.K = K; a.N = N; a.Kp = padded_k(K);
@@ -266,20 +365,16 @@ cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const 
   a.bias = bias; a.alpha = alpha; a.beta = beta;
   const int KG = a.Kp / 128;
   const int tiles = (N + 15) / 16;
-  // K-split: enough warps for ~16 per SM, and at most 4 groups (4 KB) per warp
   int S = 1;
-  while (S < 8 && S < KG && ((long long)tiles * S < 148LL * 16 || (KG + S - 1) / S > 4)) S++;
+  while (S < 8 && S < KG && ((long long)tiles * S < 148LL * 16 || (KG + S - 1) / S > 2)) S++;
+  int C = 1;
+  const int ctas = (tiles + (8 / S) - 1) / (8 / S);
+  while (C < 4 && (long long)ctas * C < 148 && KG >= 2 * S * C) C *= 2;
   a.ksplit = S;
-  const int gpw = (KG + S - 1) / S;
-  const int nt = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
-  if (layout == 1) {
-    if (nt == 1) return launch_nt<1, 1>(a, gpw, st, pdl);
-    if (nt == 2) return launch_nt<1, 2>(a, gpw, st, pdl);
-    return launch_nt<1, 4>(a, gpw, st, pdl);
-  }
-  if (nt == 1) return launch_nt<0, 1>(a, gpw, st, pdl);
-  if (nt == 2) return launch_nt<0, 2>(a, gpw, st, pdl);
-  return launch_nt<0, 4>(a, gpw, st, pdl);
+  a.csplit = C;
+  const int gpw = (KG + S * C - 1) / (S * C);
+  const int nt = M <= 8 ? 1 : (M <= 16 ? 2 : (M <= 32 ? 4 : 8));
+  return layout == 1 ? launch_layout<1>(a, nt, gpw, st, pdl) : launch_layout<0>(a, nt, gpw, st, pdl);
 }
 
 }  // namespace aria_q4

@@ -123,7 +123,7 @@ class DecodeProgram:
     def run(self, stack: Q4Stack | None = None) -> None:
         st = stack or self.stack
         for (name, w), x, y in zip(st.weights, self.xs, self.ys):
-            matmul(x, w, y)
+            matmul(x, w, y, const_weights=True)  # model weights: never written inside a step
 
     @property
     def launches(self) -> int:

@@ -129,8 +129,12 @@ class Q4Weight:
 
 
 def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bias: torch.Tensor | None = None,
-           alpha: float = 1.0, beta: float = 0.0, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
-    """y[M, N] = alpha * x[M, K] @ W + beta * out + bias, through aria_q4_0_matmul."""
+           alpha: float = 1.0, beta: float = 0.0, out_dtype: torch.dtype = torch.float16,
+           const_weights: bool = False) -> torch.Tensor:
+    """y[M, N] = alpha * x[M, K] @ W + beta * out + bias, through aria_q4_0_matmul_ex.
+
+    const_weights: the weight buffer is not written by the kernel preceding this
+    call on the stream (model weights), so the kernel may start reading it early."""
     _require_cuda(x, "x")
     if x.dtype != torch.float16:
         raise TypeError("x must be f16 (the reference's activation dtype)")
@@ -148,9 +152,10 @@ def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bia
         _require_cuda(bias, "bias")
         if bias.dtype != torch.float16 or bias.numel() != w.N:
             raise ValueError("bias must be f16 [N]")
-    call("aria_q4_0_matmul", w.buf.data_ptr(), w.layout, w.K, w.N, x2.data_ptr(), M, x2.stride(0),
+    call("aria_q4_0_matmul_ex", w.buf.data_ptr(), w.layout, w.K, w.N, x2.data_ptr(), M, x2.stride(0),
          out.data_ptr(), ydt, out.reshape(-1, w.N).stride(0),
-         bias.data_ptr() if bias is not None else None, float(alpha), float(beta), _stream(x.device))
+         bias.data_ptr() if bias is not None else None, float(alpha), float(beta),
+         _lib.FLAG_CONST_WEIGHTS if const_weights else 0, _stream(x.device))
     return out
 
 

@@ -107,6 +107,24 @@ ARIA_Q4_API int aria_q4_0_matmul(const void* tiled, int layout, int K, int N,
                      void* y, int y_dtype, int ldy,
                      const uint16_t* bias, float alpha, float beta, void* stream);
 
+/* Flags of aria_q4_0_matmul_ex. */
+enum {
+  /* The weight buffer is not written by the kernel that precedes this call on
+   * the stream (true for model weights loaded at start-up).  The projection may
+   * then read its weights before waiting for that kernel to finish, overlapping
+   * weight streaming with the previous projection's tail.  Leave it clear when
+   * the weights were just produced on the same stream (repack/quantize). */
+  ARIA_Q4_FLAG_CONST_WEIGHTS = 1
+};
+
+/* aria_q4_0_matmul with scheduling flags (ARIA_Q4_FLAG_*); flags = 0 is exactly
+ * aria_q4_0_matmul.  No reference counterpart: a launch hint for chains of
+ * projections (the reference's per-layer gemm() calls, :1583-:1864). */
+ARIA_Q4_API int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N,
+                        const uint16_t* x, int M, int ldx,
+                        void* y, int y_dtype, int ldy,
+                        const uint16_t* bias, float alpha, float beta, int flags, void* stream);
+
 /* ---------------------------------------------------------------- errors */
 
 ARIA_Q4_API const char* aria_q4_strerror(int status);

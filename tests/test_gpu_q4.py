@@ -141,7 +141,7 @@ EFKOLOS = [("qkv", LAYOUT_KN, 896, 2688), ("attn_out", LAYOUT_KN, 896, 896), ("f
 
 
 @pytest.mark.parametrize("name,layout,K,N", EFKOLOS)
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 16])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 16, 24, 40, 64])
 def test_efkolos_projections(q4, coracle, name, layout, K, N, M):
     if name == "lm_head" and M > 4:
         pytest.skip("fp64 oracle too slow for this size; covered at M<=4")
@@ -184,3 +184,29 @@ def test_errors_are_raised(q4):
     with pytest.raises(AriaQ4Error) as ei:
         q4.Q4Weight.from_f16(torch.zeros(64, 48, dtype=torch.float16, device="cuda"), LAYOUT_KN)
     assert ei.value.status == 2
+
+
+@pytest.mark.parametrize("name,layout,K,N", EFKOLOS)
+def test_const_weights_flag_same_result(q4, name, layout, K, N):
+    """aria_q4_0_matmul_ex with ARIA_Q4_FLAG_CONST_WEIGHTS computes exactly what
+    aria_q4_0_matmul computes (only the load schedule differs)."""
+    from aria_b200.efkolos import synth_f16
+    shape = (K, N) if layout == LAYOUT_KN else (N, K)
+    wq = q4.Q4Weight.from_f16(synth_f16(shape, 0.02, 3), layout)
+    for M in (1, 3, 16):
+        x = synth_f16((M, K), 1.0, 4)
+        torch.cuda.synchronize()
+        a = q4.matmul(x, wq, out_dtype=torch.float32)
+        b = q4.matmul(x, wq, out_dtype=torch.float32, const_weights=True)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b), (name, M)
+
+
+def test_matmul_ex_rejects_unknown_flags(q4):
+    from aria_b200._lib import lib
+    w = q4.Q4Weight.from_f16(torch.zeros(64, 64, dtype=torch.float16, device="cuda"), LAYOUT_KN)
+    x = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
+    y = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
+    rc = lib().aria_q4_0_matmul_ex(w.buf.data_ptr(), 0, 64, 64, x.data_ptr(), 1, 64, y.data_ptr(), 1, 64, None,
+                                   1.0, 0.0, 6, None)
+    assert rc == 1
