@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill", type=lambda v: [int(t) for t in v.split(",") if t], default=[4096, 8192])
     ap.add_argument("--batched", type=lambda v: [int(t) for t in v.split(",") if t], default=[16, 64, 256])
+    ap.add_argument("--scaled", type=int, default=1, help="1: also run BASELINE configs[4] (d_model 4096)")
+    ap.add_argument("--scaled-prefill-tokens", type=int, default=4096)
     return ap.parse_args()
 
 
@@ -168,6 +170,51 @@ def run_reference(args, rank: int) -> None:
 
 
 # ------------------------------------------------------------------ GPU arm
+
+def scaled_section(args, rank, world, local_rank, stream, timed, peaks):
+    """decode batch 64 with column-split FFN / LM head and NCCL
+    all-gathers, and batch-sharded prefill (4096 tokens per rank per step)."""
+    import torch
+    from aria_b200.efkolos import SCALED, DecodeProgram, Q4Stack
+    from aria_b200.scaled import ColumnSplitDecode
+    out = {"workload": "BASELINE configs[4]: 32 layers, d_model 4096, FFN 16384, vocab 31500"}
+    prog = ColumnSplitDecode(SCALED, M=64, world=world, rank=rank)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        prog.run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            prog.run()
+    steps = max(5, args.steps // 10)
+    ms = timed(lambda i: g.replay(), steps, 3, "aria_scaled_decode") / steps
+    wb = prog.weight_bytes()
+    out["decode_b64_colsplit"] = {
+        "ms_per_step": ms, "tokens_per_s": 64 / (ms * 1e-3),
+        "weight_GBs_per_rank": wb / (ms * 1e-3) / 1e9, "weight_GBs_total": wb * world / (ms * 1e-3) / 1e9,
+        "allgather_bytes_in_per_rank": prog.gathered_bytes(),
+        "split": "ffn_up, ffn_down, LM head column-split over ranks; QKV, attn_out replicated"}
+    del g, prog
+    torch.cuda.empty_cache()
+    stack = Q4Stack.build(SCALED, seed=rank * 1000 + 77)
+    M = args.scaled_prefill_tokens
+    pprog = DecodeProgram(stack, M=M, seed=rank + 31)
+    with torch.cuda.stream(stream):
+        pprog.run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            pprog.run()
+    pms = timed(lambda i: g.replay(), 3, 2, "aria_scaled_prefill") / 3
+    tf = M * SCALED.flops_per_token() * world / (pms * 1e-3) / 1e12
+    out["prefill_batch_sharded"] = {
+        "tokens_per_rank_per_step": M, "ms_per_step": pms, "tokens_per_s": M * world / (pms * 1e-3),
+        "TFLOPs": tf, "frac_of_measured_bf16_peak": tf / world / float(peaks.get("bf16_tflops", 1590.0)),
+        "job": "256 x 512 tokens split by batch; each step is a bounded sample of M tokens per rank"}
+    del g, pprog, stack
+    torch.cuda.empty_cache()
+    return out
+
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch
@@ -329,6 +376,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                             "frac_of_measured_sustained_peak": tf / world / bf16_sus}
         del g, pprog
         torch.cuda.empty_cache()
+    scaled = None
+    if args.scaled:
+        scaled = scaled_section(args, rank, world, local_rank, stream, timed, peaks)
     clocks = sampler.stop()
 
     cpu = None
@@ -350,6 +400,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                    "tokens (8x512 = 4096, 4x2048 = 8192), tcgen05 kernel",
                        "flops_per_token": flops_token, "peak_tflops_measured": bf16_peak,
                        "peak_tflops_sustained": bf16_sus, **prefill},
+           "scaled": scaled,
            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": prog.input_bytes(),
                    "d2h_bytes_per_step": prog.ys[-1].numel() * 2, "ms_per_step": e2e_ms},
            "gpu_launches": prog.launches * args.steps}
