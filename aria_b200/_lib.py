@@ -17,6 +17,8 @@ LIB_PATH = os.path.join(_PKG, "libaria_q4.so")
 OK, EINVAL, EUNSUPPORTED, EALIGN, ECUDA, ENODEVICE, ESIZE = range(7)
 LAYOUT_KN, LAYOUT_NK = 0, 1
 FLAG_CONST_WEIGHTS = 1
+FLAG_KERNEL_STREAM = 2
+FLAG_KERNEL_REGISTER = 4
 F32, F16 = 0, 1
 
 # every symbol include/aria_q4.h declares: (restype, argtypes)

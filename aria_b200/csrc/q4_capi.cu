@@ -1,7 +1,8 @@
 // q4_capi.cu -- extern "C" entry points of libaria_q4.so (declared in
 // include/aria_q4.h).  Argument checking, status codes and kernel selection;
-// the kernels live in q4_pack.cu, q4_decode.cu and q4_gemm_tc.cu.
+// the kernels live in q4_pack.cu, q4_gemv.cu, q4_decode.cu and q4_gemm_tc.cu.
 #include <cstdio>
+#include <cstdlib>
 
 #include "../../include/aria_q4.h"
 #include "q4_common.cuh"
@@ -15,6 +16,10 @@ cudaError_t launch_quantize_tiled(const uint16_t* w, int layout, int K, int N, u
 cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                           int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
                           bool const_weights);
+bool gemv_supported(int K, int N, int M);
+cudaError_t launch_gemv(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
+                        int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
+                        bool const_weights);
 cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                            int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl);
 int take_device_error();
@@ -26,6 +31,17 @@ int take_device_error();
 #define ARIA_Q4_DECODE_MAX_M 64
 #endif
 static const int kDecodeMaxM = ARIA_Q4_DECODE_MAX_M;
+
+// Default decode-kernel choice: the streaming GEMV for M <= 8 when the weight
+// is at least kStreamMinBytesPerSm of packed bytes per SM (below that a
+// projection is latency-bound and the register-fed kernel, with its smaller
+// CTAs, overlaps better with its neighbours in a chain of projections).
+static const double kStreamMinBytesPerSm = 32.0 * 1024;
+static bool stream_by_default(int K, int N, int M) {
+  if (M > 8) return false;
+  const double per_sm = (double)N * (aria_q4::padded_k(K) / 128) * 72.0 / 148.0;
+  return per_sm >= kStreamMinBytesPerSm && aria_q4::gemv_supported(K, N, M);
+}
 
 using namespace aria_q4;
 
@@ -120,18 +136,28 @@ int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N, const uint1
   if (!tiled || !x || !y) return ARIA_Q4_EINVAL;
   if (y_dtype != ARIA_Q4_F16 && y_dtype != ARIA_Q4_F32) return ARIA_Q4_EINVAL;
   if (ldx < K || ldy < N) return ARIA_Q4_EINVAL;
-  if ((flags & ~ARIA_Q4_FLAG_CONST_WEIGHTS) != 0) return ARIA_Q4_EINVAL;
+  const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_STREAM | ARIA_Q4_FLAG_KERNEL_REGISTER;
+  if ((flags & ~known) != 0) return ARIA_Q4_EINVAL;
+  const bool want_stream = (flags & ARIA_Q4_FLAG_KERNEL_STREAM) != 0;
+  const bool want_register = (flags & ARIA_Q4_FLAG_KERNEL_REGISTER) != 0;
+  if (want_stream && want_register) return ARIA_Q4_EINVAL;
   if (((uintptr_t)tiled & 255u) != 0 || !aligned16(x) || (ldx % 8) != 0) return ARIA_Q4_EALIGN;
   if (int s = check_device()) return s;
   const cudaStream_t st = (cudaStream_t)stream;
-  // Kernel choice: the register-fed decode kernel up to 32 tokens (and up to 64
-  // when the output has too few 128-row tiles to fill the GPU with tcgen05 work);
-  // the tcgen05 kernel above that.
-  const bool decode = M <= 32 || (M <= kDecodeMaxM && N < 8192);
+  // Kernel choice: the streaming GEMV for M <= 8 and large weights; the
+  // register-fed decode kernel up to 32 tokens (and up to 64 when the output has
+  // too few 128-row tiles to fill the GPU with tcgen05 work); the tcgen05
+  // kernel above that.  ARIA_Q4_FLAG_KERNEL_* overrides the first two.
+  const bool cw = (flags & ARIA_Q4_FLAG_CONST_WEIGHTS) != 0;
+  if (want_stream && !gemv_supported(K, N, M)) return ARIA_Q4_EUNSUPPORTED;
+  if (want_register && M > kDecodeMaxM) return ARIA_Q4_EUNSUPPORTED;
+  if (want_stream || (!want_register && stream_by_default(K, N, M)))
+    return cuda_status(launch_gemv((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
+                                   (const __half*)bias, alpha, beta, st, true, cw));
+  const bool decode = want_register || M <= 32 || (M <= kDecodeMaxM && N < 8192);
   if (decode)
     return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
-                                     (const __half*)bias, alpha, beta, st, true,
-                                     (flags & ARIA_Q4_FLAG_CONST_WEIGHTS) != 0));
+                                     (const __half*)bias, alpha, beta, st, true, cw));
   return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
                                     (const __half*)bias, alpha, beta, st, true));
 }

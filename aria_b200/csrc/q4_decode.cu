@@ -53,30 +53,6 @@ struct DecodeArgs {
   int const_weights;  // weights are not written by the preceding kernel: load them before the dependency wait
 };
 
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t a0, const uint32_t a1, const uint32_t a2,
-                                          const uint32_t a3, const uint32_t b0, const uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void store_out(void* y, int ydt, size_t idx, float v, float beta) {
-  if (ydt == 0) {
-    float* yp = reinterpret_cast<float*>(y) + idx;
-    if (beta != 0.0f) v += beta * *yp;
-    *yp = v;
-  } else {
-    __half* yp = reinterpret_cast<__half*>(y) + idx;
-    if (beta != 0.0f) v += beta * __half2float(*yp);
-    *yp = __float2half_rn(v);
-  }
-}
-
 __device__ __forceinline__ uint4 ld_u4_or(const void* p, bool ok, uint32_t fill) {
   return ok ? ld_weights_u4(p) : make_uint4(fill, fill, fill, fill);
 }
@@ -91,17 +67,6 @@ struct GroupRegs {
   uint4 xv[PRE ? 4 : 1][PRE ? NT : 1];
   uint4 ks[PRE ? 4 : 1];
 };
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ float ld_dsmem_f32(const float* local_addr, uint32_t rank) {
-  uint32_t remote, v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(tc_smem_u32(local_addr)), "r"(rank));
-  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
-  return __uint_as_float(v);
-}
 
 // PRE: the batch phase also loads every activation / KN-scale fragment of its
 // groups (small NT), so no load latency is exposed inside the MMA loop.

@@ -128,13 +128,18 @@ class Q4Weight:
         return q
 
 
+_KERNEL_FLAGS = {"auto": 0, "stream": _lib.FLAG_KERNEL_STREAM, "register": _lib.FLAG_KERNEL_REGISTER}
+
+
 def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bias: torch.Tensor | None = None,
            alpha: float = 1.0, beta: float = 0.0, out_dtype: torch.dtype = torch.float16,
-           const_weights: bool = False) -> torch.Tensor:
+           const_weights: bool = False, kernel: str = "auto") -> torch.Tensor:
     """y[M, N] = alpha * x[M, K] @ W + beta * out + bias, through aria_q4_0_matmul_ex.
 
     const_weights: the weight buffer is not written by the kernel preceding this
-    call on the stream (model weights), so the kernel may start reading it early."""
+    call on the stream (model weights), so the kernel may start reading it early.
+    kernel: "auto" (the library chooses), "stream" (streaming GEMV, M <= 8) or
+    "register" (register-fed decode kernel, M <= 64)."""
     _require_cuda(x, "x")
     if x.dtype != torch.float16:
         raise TypeError("x must be f16 (the reference's activation dtype)")
@@ -155,7 +160,7 @@ def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bia
     call("aria_q4_0_matmul_ex", w.buf.data_ptr(), w.layout, w.K, w.N, x2.data_ptr(), M, x2.stride(0),
          out.data_ptr(), ydt, out.reshape(-1, w.N).stride(0),
          bias.data_ptr() if bias is not None else None, float(alpha), float(beta),
-         _lib.FLAG_CONST_WEIGHTS if const_weights else 0, _stream(x.device))
+         (_lib.FLAG_CONST_WEIGHTS if const_weights else 0) | _KERNEL_FLAGS[kernel], _stream(x.device))
     return out
 
 

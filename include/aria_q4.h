@@ -114,7 +114,14 @@ enum {
    * then read its weights before waiting for that kernel to finish, overlapping
    * weight streaming with the previous projection's tail.  Leave it clear when
    * the weights were just produced on the same stream (repack/quantize). */
-  ARIA_Q4_FLAG_CONST_WEIGHTS = 1
+  ARIA_Q4_FLAG_CONST_WEIGHTS = 1,
+  /* Kernel selection (at most one; without either the library chooses).
+   * STREAM: the streaming GEMV (M <= 8; each warp streams packed chunks through a
+   * shared-memory ring; best for weights of tens of MB).  REGISTER: the
+   * register-fed decode kernel (M <= 64; lowest latency for small weights).
+   * ARIA_Q4_EUNSUPPORTED when the chosen kernel cannot take the shape. */
+  ARIA_Q4_FLAG_KERNEL_STREAM = 2,
+  ARIA_Q4_FLAG_KERNEL_REGISTER = 4
 };
 
 /* aria_q4_0_matmul with scheduling flags (ARIA_Q4_FLAG_*); flags = 0 is exactly

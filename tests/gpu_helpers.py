@@ -70,3 +70,47 @@ def check_close(y, ref, max_abs=1e-2, rel_l2=1e-3, what=""):
     assert mx <= max_abs, f"{what}: max-abs {mx:.3e} > {max_abs}"
     assert rl2 <= rel_l2, f"{what}: rel-L2 {rl2:.3e} > {rel_l2}"
     return mx, rl2
+
+
+def run_projection(q4, coracle, layout, K, N, M, out_dtype=None, bias=False, alpha=1.0, beta=0.0, seed=0,
+                   wscale=0.02, ldx=None, flags=0):
+    """One aria_q4_0_matmul call on seeded inputs, checked for canary damage;
+    returns (y, fp64 reference).  ldx > K leaves a gap after each x row."""
+    import torch
+    if out_dtype is None:
+        out_dtype = torch.float32
+    ldx = K if ldx is None else ldx
+    rng = np.random.default_rng(seed + 1000 * M + K + N)
+    shape = (K, N) if layout == LAYOUT_KN else (N, K)
+    w = (rng.standard_normal(shape) * wscale).astype(np.float16)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float16) if bias else None
+    blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
+    ref = coracle.matmul_ref(blocks, layout, K, N, x, b, alpha)
+    wq = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
+    # canaries: extra rows and columns around the output must stay untouched
+    ldy = N + 8
+    y0 = (rng.standard_normal((M + 2, ldy))).astype(np.float32)
+    yt = torch.from_numpy(y0).to(out_dtype).cuda()
+    view = yt[1:M + 1, :N]
+    from aria_b200._lib import call
+    from aria_b200.q4 import _stream
+    xpad = np.full((M, ldx), np.float16(np.nan), dtype=np.float16)  # the gap must never be read
+    xpad[:, :K] = x
+    xt = torch.from_numpy(xpad).cuda()
+    bt = torch.from_numpy(b).cuda() if b is not None else None
+    args = (wq.buf.data_ptr(), layout, K, N, xt.data_ptr(), M, ldx, view.data_ptr(),
+            0 if out_dtype == torch.float32 else 1, ldy, bt.data_ptr() if bt is not None else None,
+            float(alpha), float(beta))
+    if flags:
+        call("aria_q4_0_matmul_ex", *args, flags, _stream())
+    else:
+        call("aria_q4_0_matmul", *args, _stream())
+    out = yt.cpu().to(torch.float64).numpy()
+    y_init = torch.from_numpy(y0).to(out_dtype).to(torch.float64).numpy()
+    if beta != 0.0:
+        ref = ref + beta * y_init[1:M + 1, :N]
+    # canaries
+    assert np.array_equal(out[0], y_init[0]) and np.array_equal(out[M + 1], y_init[M + 1]), "row canary"
+    assert np.array_equal(out[1:M + 1, N:], y_init[1:M + 1, N:]), "column canary"
+    return out[1:M + 1, :N], ref

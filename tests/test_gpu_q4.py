@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import q4_oracle_np as npo
-from tests.gpu_helpers import LAYOUT_KN, LAYOUT_NK, check_close, tiled_from_aos, tiled_regions
+from tests.gpu_helpers import LAYOUT_KN, LAYOUT_NK, check_close, run_projection, tiled_from_aos, tiled_regions
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")]
@@ -98,36 +98,7 @@ def test_repack_and_quantize_tiled(q4, coracle, layout, K, N):
 
 # ------------------------------------------------------------------ projections
 
-def _run(q4, coracle, layout, K, N, M, out_dtype=torch.float32, bias=False, alpha=1.0, beta=0.0, seed=0,
-         wscale=0.02):
-    rng = np.random.default_rng(seed + 1000 * M + K + N)
-    shape = (K, N) if layout == LAYOUT_KN else (N, K)
-    w = (rng.standard_normal(shape) * wscale).astype(np.float16)
-    x = rng.standard_normal((M, K)).astype(np.float16)
-    b = (rng.standard_normal(N) * 0.1).astype(np.float16) if bias else None
-    blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
-    ref = coracle.matmul_ref(blocks, layout, K, N, x, b, alpha)
-    wq = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
-    # canaries: extra rows and columns around the output must stay untouched
-    ldy = N + 8
-    y0 = (rng.standard_normal((M + 2, ldy))).astype(np.float32)
-    yt = torch.from_numpy(y0).to(out_dtype).cuda()
-    view = yt[1:M + 1, :N]
-    from aria_b200._lib import call
-    from aria_b200.q4 import _stream
-    xt = torch.from_numpy(x).cuda()
-    bt = torch.from_numpy(b).cuda() if b is not None else None
-    call("aria_q4_0_matmul", wq.buf.data_ptr(), layout, K, N, xt.data_ptr(), M, K, view.data_ptr(),
-         0 if out_dtype == torch.float32 else 1, ldy, bt.data_ptr() if bt is not None else None,
-         float(alpha), float(beta), _stream())
-    out = yt.cpu().to(torch.float64).numpy()
-    y_init = torch.from_numpy(y0).to(out_dtype).to(torch.float64).numpy()
-    if beta != 0.0:
-        ref = ref + beta * y_init[1:M + 1, :N]
-    # canaries
-    assert np.array_equal(out[0], y_init[0]) and np.array_equal(out[M + 1], y_init[M + 1]), "row canary"
-    assert np.array_equal(out[1:M + 1, N:], y_init[1:M + 1, N:]), "column canary"
-    return out[1:M + 1, :N], ref
+_run = run_projection
 
 
 def test_config0_single_projection(q4, coracle):
@@ -208,5 +179,5 @@ def test_matmul_ex_rejects_unknown_flags(q4):
     x = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
     y = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
     rc = lib().aria_q4_0_matmul_ex(w.buf.data_ptr(), 0, 64, 64, x.data_ptr(), 1, 64, y.data_ptr(), 1, 64, None,
-                                   1.0, 0.0, 6, None)
+                                   1.0, 0.0, 8, None)
     assert rc == 1
