@@ -123,12 +123,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::mbar_init(&empty_x[s], 1);
     }
     for (int s = 0; s < kASlots; s++) {
-      tc::mbar_init(&full_a[s], 128);
+      tc::mbar_init(&full_a[s], 4);  // one arrival per dequant warp
       tc::mbar_init(&empty_a[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       tc::mbar_init(&acc_full[b], 1);
-      tc::mbar_init(&acc_empty[b], 128);
+      tc::mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
@@ -216,11 +216,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------------------------------------ dequantisers
     // Two warpgroups: WG w (warps 4w..4w+3) owns the 128-k groups G = w, w+2, ...
     // of every tile and feeds both of their 64-k stages.  Each thread owns one
-    // weight row (= TMEM lane) and streams the row's 64-byte code group plus its
-    // scales into a kQDepth-deep shared-memory ring with 16-byte cp.async, so
-    // loads run groups ahead without holding registers; the four 16-byte chunks
-    // of a row are stored XOR-swizzled by (row >> 1) & 3 so neighbouring rows'
-    // 128-bit reads hit distinct banks.  KN scales (one per k for a 32-row
+    // weight row (= TMEM lane); each warp streams its 32 rows' 64-byte code
+    // groups plus their scales into a kQDepth-deep shared-memory ring with
+    // 16-byte cp.async, so loads run groups ahead without holding registers; the
+    // four 16-byte chunks of a row are stored XOR-swizzled by (row >> 1) & 3 so
+    // neighbouring rows' 128-bit reads hit distinct banks.  KN scales (one per k for a 32-row
     // group) are shared by a warp: lanes 0..15 copy the group's 256 bytes.
     const int wg = warp >> 2;         // 0 or 1
     const int wl = warp & 3;          // warp within the warpgroup = TMEM lane quadrant
@@ -238,13 +238,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int j = seq / gpt, G = wg + 2 * (seq % gpt);
         const int tile = blockIdx.x + j * gridDim.x;
         const int nb = (tile % n_tiles) * 128;
+        // codes: the warp copies its 32 rows cooperatively, lane l taking 16-byte
+        // chunk l % 4 of row 8u + l / 4, so one copy instruction reads eight whole
+        // 64-byte row segments (instead of 32 scattered 16-byte pieces)
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int rl = 32 * wl + 8 * u + (lane >> 2);
+          const int q = lane & 3;
+          const int nr = nb + rl;
+          const bool okr = nr < a.N;
+          cp_async_16(qring + slot * kQSlot + rl * 64 + ((q ^ ((rl >> 1) & 3)) << 4),
+                      a.qs + (okr ? (size_t)nr : 0) * RB + (size_t)G * 64 + 16 * q, okr);
+        }
         const int n = nb + r;
         const bool ok_row = n < a.N;
         const size_t nn = ok_row ? (size_t)n : 0;
-        const uint8_t* src = a.qs + nn * RB + (size_t)G * 64;
-        uint8_t* dst = qring + slot * kQSlot + r * 64;
-#pragma unroll
-        for (int q = 0; q < 4; q++) cp_async_16(dst + ((q ^ sw) << 4), src + 16 * q, ok_row);
         if (LAYOUT == 1) {
           cp_async_8(sring + slot * kSSlot + r * 8, a.scales + ((size_t)G * a.N + nn) * 4, ok_row);
         } else if (lane < 16) {
@@ -281,7 +289,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (kt >= KT) break;
           const int c = acnt++;
           const int s = wg * kAPer + c % kAPer;  // A slot in this warpgroup's sub-ring
-          if (c >= kAPer && !tc::mbar_wait(&empty_a[s], ((c / kAPer) - 1) & 1)) {
+          // warp-uniform outcome: tcgen05.st and the per-warp arrival below are warp-collective
+          if (c >= kAPer && !__all_sync(0xffffffffu, tc::mbar_wait(&empty_a[s], ((c / kAPer) - 1) & 1))) {
             tc::record_error(tc::kErrTimeoutEmpty);
             ok = false;
             break;
@@ -317,7 +326,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                  av);
           tc::tmem_st_wait();
           tc::tc_fence_before();
-          tc::mbar_arrive(&full_a[s]);
+          __syncwarp();  // the warp's 32 lanes have stored: one arrival for the warp
+          if (lane == 0) tc::mbar_arrive(&full_a[s]);
         }
       }
     }
@@ -332,11 +342,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int tile = blockIdx.x + j * gridDim.x;
       const int n = (tile % n_tiles) * 128 + rr;
       const int m0 = (tile / n_tiles) * BT;
-      if (!tc::mbar_wait(&acc_full[buf], (j >> 1) & 1)) {
+      // warp-uniform decisions: the per-warp arrival below is reached by all lanes or none
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[buf], (j >> 1) & 1))) {
         tc::record_error(tc::kErrTimeoutAccum);
         break;
       }
-      if (*reinterpret_cast<volatile int*>(abort_flag) != 0) break;
+      if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abort_flag) != 0)) break;
       tc::tc_fence_after();
       const bool row_ok = n < a.N;
       const float bias = (a.bias && row_ok) ? __half2float(a.bias[n]) : 0.0f;
@@ -378,7 +389,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       tc::tc_fence_before();
-      tc::mbar_arrive(&acc_empty[buf]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
     }
   }
 
