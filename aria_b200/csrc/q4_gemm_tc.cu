@@ -94,7 +94,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // TMEM: two f32 accumulators [128 x BT] then kASlots dequantised A stages
-  constexpr int kASlots = (512 - 2 * BT) / kAStageCols >= 8 ? 8 : 4;  // two sub-rings of kASlots/2
+  // every free TMEM column holds A stages (up to 12): each dequant warpgroup's
+  // sub-ring depth bounds how many stages are in flight between dequantisation
+  // and MMA completion, which sets the stage rate when few tokens make each
+  // MMA short (measured: 64 stages per tile at BT = 64 ran at ~600 cycles each
+  // with four slots in all)
+  constexpr int kASlots = (512 - 2 * BT) / kAStageCols >= 12 ? 12 : ((512 - 2 * BT) / kAStageCols) & ~1;
   constexpr int kAPer = kASlots / 2;
   constexpr uint32_t kAColBase = 2 * BT;
   constexpr uint32_t kNeed = 2 * BT + kASlots * kAStageCols;
@@ -173,8 +178,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(128, BT);
-      int it = 0;
-      int acnt0 = 0, acnt1 = 0;  // stages consumed from each warpgroup's A sub-ring
+      // The issuing thread's per-stage work is the MMA pipe's throughput limit
+      // (every tcgen05 and mbarrier operation costs tens of cycles of issue
+      // latency), so ring positions advance incrementally and descriptors are
+      // derived from one precomputed base: no divisions or descriptor
+      // rebuilding inside the loop.
+      const uint64_t desc0 = tc::sdesc_k_sw128(tc::smem_u32(smem));  // X slot 0; address field in 16-B units
+      int xslot = 0;
+      uint32_t xph = 0;
+      int aslot0 = 0, aslot1 = 0;  // position in each warpgroup's A sub-ring
+      uint32_t aph0 = 0, aph1 = 0;
       bool ok = true;
       for (int j = 0; j < my_tiles && ok; j++) {
         const int buf = j & 1;
@@ -185,28 +198,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc::tc_fence_after();
         const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT);
-        for (int kt = 0; kt < KT; kt++, it++) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
+        for (int kt = 0; kt < KT; kt++) {
           const int w = (kt >> 1) & 1;  // warpgroup that dequantised this stage
-          const int c = w ? acnt1++ : acnt0++;
-          const int as = w * kAPer + c % kAPer;
-          const uint32_t aph = (c / kAPer) & 1;
-          if (!tc::mbar_wait(&full_x[s], ph) || !tc::mbar_wait(&full_a[as], aph)) {
+          const int as = w ? kAPer + aslot1 : aslot0;
+          const uint32_t aph = w ? aph1 : aph0;
+          if (w) {
+            if (++aslot1 == kAPer) { aslot1 = 0; aph1 ^= 1u; }
+          } else {
+            if (++aslot0 == kAPer) { aslot0 = 0; aph0 ^= 1u; }
+          }
+          if (!tc::mbar_wait(&full_x[xslot], xph) || !tc::mbar_wait(&full_a[as], aph)) {
             tc::record_error(tc::kErrTimeoutFull);
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const uint32_t xs = tc::smem_u32(smem + s * L::kStage);
+          const uint64_t bdesc = desc0 + (uint64_t)((uint32_t)(xslot * L::kStage) >> 4);
           const uint32_t at = tmem_base + kAColBase + (uint32_t)(as * kAStageCols);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; kk++) {
-            const uint64_t bdesc = tc::sdesc_k_sw128(xs + kk * 32);
-            tc::umma_f16_ta(tmem_d, at + (uint32_t)(kk * 8), bdesc, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc::umma_commit(&empty_x[s]);
+          for (int kk = 0; kk < kBK / 16; kk++)
+            tc::umma_f16_ta(tmem_d, at + (uint32_t)(kk * 8), bdesc + (uint64_t)(kk * 2), idesc,
+                            (kt > 0 || kk > 0) ? 1u : 0u);
+          tc::umma_commit(&empty_x[xslot]);
           tc::umma_commit(&empty_a[as]);
+          if (++xslot == STAGES) { xslot = 0; xph ^= 1u; }
         }
         tc::umma_commit(&acc_full[buf]);  // also on the error path, so the epilogue is released
       }
