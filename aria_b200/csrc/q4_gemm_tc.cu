@@ -87,7 +87,7 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int LAYOUT, int BT, int STAGES>
+template <int LAYOUT, int BT, int STAGES, int NACC>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const TcArgs a, int n_tiles, int num_tiles) {
   using L = TcSmem<BT, STAGES>;
@@ -99,12 +99,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // and MMA completion, which sets the stage rate when few tokens make each
   // MMA short (measured: 64 stages per tile at BT = 64 ran at ~600 cycles each
   // with four slots in all)
-  constexpr int kASlots = (512 - 2 * BT) / kAStageCols >= 12 ? 12 : ((512 - 2 * BT) / kAStageCols) & ~1;
+  // NACC = 2 accumulators let the next tile's MMAs overlap this tile's
+  // epilogue; NACC = 1 leaves TMEM room for token tiles up to 256 (for shapes
+  // whose tiles fit one round of CTAs there is no next tile to overlap).
+  constexpr int kFreeCols = 512 - NACC * BT;
+  constexpr int kASlots = kFreeCols / kAStageCols >= 12 ? 12 : (kFreeCols / kAStageCols) & ~1;
+  static_assert(kASlots >= 4, "two A slots per dequant warpgroup");
   constexpr int kAPer = kASlots / 2;
-  constexpr uint32_t kAColBase = 2 * BT;
-  constexpr uint32_t kNeed = 2 * BT + kASlots * kAStageCols;
+  constexpr uint32_t kAColBase = NACC * BT;  // A stages follow the accumulators
+  constexpr uint32_t kNeed = NACC * BT + kASlots * kAStageCols;
   constexpr uint32_t kCols = kNeed <= 32 ? 32 : kNeed <= 64 ? 64 : kNeed <= 128 ? 128 : kNeed <= 256 ? 256 : 512;
   static_assert(kNeed <= 512, "TMEM budget");
+  static_assert(kAColBase + kASlots * kAStageCols <= kCols, "A stages inside the allocation");
   // X tiles: one ring indexed by the CTA's stage counter (producer and MMA walk it
   // in order).  Dequantised A stages: two private sub-rings of kASlots/2, one per
   // dequant warpgroup, indexed by that warpgroup's own stage counter -- so no
@@ -190,8 +196,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t aph0 = 0, aph1 = 0;
       bool ok = true;
       for (int j = 0; j < my_tiles && ok; j++) {
-        const int buf = j & 1;
-        if (j >= 2 && !tc::mbar_wait(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
+        const int buf = NACC == 2 ? (j & 1) : 0;
+        const int use = NACC == 2 ? (j >> 1) : j;  // earlier uses of this accumulator
+        if (use >= 1 && !tc::mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
           tc::record_error(tc::kErrTimeoutAccum);
           ok = false;
           break;
@@ -353,12 +360,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int rr = q * 32 + lane;
     for (int j = 0; j < my_tiles; j++) {
-      const int buf = j & 1;
+      const int buf = NACC == 2 ? (j & 1) : 0;
+      const int use = NACC == 2 ? (j >> 1) : j;
       const int tile = blockIdx.x + j * gridDim.x;
       const int n = (tile % n_tiles) * 128 + rr;
       const int m0 = (tile / n_tiles) * BT;
       // warp-uniform decisions: the per-warp arrival below is reached by all lanes or none
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[buf], (j >> 1) & 1))) {
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[buf], use & 1))) {
         tc::record_error(tc::kErrTimeoutAccum);
         break;
       }
@@ -435,7 +443,7 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-template <int LAYOUT, int BT, int STAGES>
+template <int LAYOUT, int BT, int STAGES, int NACC>
 static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaStream_t st, bool pdl) {
   using L = TcSmem<BT, STAGES>;
   EncodeTiledFn enc = get_encode_fn();
@@ -449,7 +457,7 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  auto kern = gemm_tc_kernel<LAYOUT, BT, STAGES>;
+  auto kern = gemm_tc_kernel<LAYOUT, BT, STAGES, NACC>;
   static bool attr_set = false;  // idempotent; a racing second set is harmless
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
@@ -486,15 +494,50 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
   a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;
   a.y = y; a.ydt = ydt; a.ldy = ldy; a.bias = bias; a.alpha = alpha; a.beta = beta;
-  // BT (tokens per tile) x STAGES under the TMEM budget 2*BT + 32*STAGES <= 512
-  if (layout == 1) {
-    if (M <= 64) return launch_tc_t<1, 64, 8>(a, x, ldx, st, pdl);
-    if (M <= 128) return launch_tc_t<1, 128, 8>(a, x, ldx, st, pdl);
-    return launch_tc_t<1, 192, 4>(a, x, ldx, st, pdl);
+  // Token-tile height BT by a cost model: rounds of CTAs (tiles / SMs, rounded
+  // up) x 64-k stages per tile x (fixed issue cost of a stage + 2 cycles per
+  // token), plus, for a single accumulator, the exposed epilogue of every round
+  // after the first.  The fixed ~450 cycles per stage is the MMA issuer's
+  // latency (two barrier waits, a fence, four MMAs and two commits).
+  static int num_sms = 0;
+  if (num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (num_sms <= 0) num_sms = 148;
   }
-  if (M <= 64) return launch_tc_t<0, 64, 8>(a, x, ldx, st, pdl);
-  if (M <= 128) return launch_tc_t<0, 128, 8>(a, x, ldx, st, pdl);
-  return launch_tc_t<0, 192, 4>(a, x, ldx, st, pdl);
+  struct Cand { int bt, nacc; };
+  const Cand cands[] = {{64, 2}, {128, 2}, {192, 2}, {224, 1}, {256, 1}};
+  const long long n_tiles = (N + 127) / 128;
+  const long long KT = (K + kBK - 1) / kBK;
+  int best_bt = 64;
+  long long best = -1;
+  for (const Cand& c : cands) {
+    if (c.bt > 64 && M <= 64) break;
+    const long long tiles = n_tiles * ((M + c.bt - 1) / c.bt);
+    const long long rounds = (tiles + num_sms - 1) / num_sms;
+    const long long cost = rounds * KT * (450 + 2 * c.bt) + (c.nacc == 1 ? (rounds - 1) * 8 * c.bt : 0);
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_bt = c.bt;
+    }
+  }
+  if (layout == 1) {
+    switch (best_bt) {
+      case 64: return launch_tc_t<1, 64, 8, 2>(a, x, ldx, st, pdl);
+      case 128: return launch_tc_t<1, 128, 8, 2>(a, x, ldx, st, pdl);
+      case 192: return launch_tc_t<1, 192, 4, 2>(a, x, ldx, st, pdl);
+      case 224: return launch_tc_t<1, 224, 4, 1>(a, x, ldx, st, pdl);
+      default: return launch_tc_t<1, 256, 4, 1>(a, x, ldx, st, pdl);
+    }
+  }
+  switch (best_bt) {
+    case 64: return launch_tc_t<0, 64, 8, 2>(a, x, ldx, st, pdl);
+    case 128: return launch_tc_t<0, 128, 8, 2>(a, x, ldx, st, pdl);
+    case 192: return launch_tc_t<0, 192, 4, 2>(a, x, ldx, st, pdl);
+    case 224: return launch_tc_t<0, 224, 4, 1>(a, x, ldx, st, pdl);
+    default: return launch_tc_t<0, 256, 4, 1>(a, x, ldx, st, pdl);
+  }
 }
 
 // Reads and clears the device error flag (synchronous).

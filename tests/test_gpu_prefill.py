@@ -88,6 +88,24 @@ def test_prefill_full_size_sampled_rows(q4, coracle, name, layout, K, N):
     assert np.isfinite(y).all()
 
 
+@pytest.mark.parametrize("layout,K,N,M", [
+    (LAYOUT_KN, 256, 1152, 4096),   # 9 row tiles: 256-token tiles fit one round of CTAs (single accumulator)
+    (LAYOUT_NK, 320, 896, 4096),    # 7 row tiles: 224-token tiles (single accumulator)
+    (LAYOUT_KN, 224, 896, 8192),    # two rounds of 224-token tiles
+    (LAYOUT_NK, 256, 3584, 4096),   # 192-token tiles, double-buffered accumulators
+    (LAYOUT_KN, 192, 640, 128),     # 128-token tiles
+])
+def test_prefill_token_tile_variants(q4, coracle, layout, K, N, M):
+    """Every token-tile height the launcher can choose, with sampled rows
+    (first, last and a seeded sample) checked against fp64."""
+    w, blocks, W = _weights(coracle, layout, K, N, seed=K + 3 * N + M)
+    x = np.random.default_rng(M + N).standard_normal((M, K)).astype(np.float16)
+    y = _run(q4, w, layout, x, out_dtype=torch.float32)
+    rows = np.random.default_rng(5).choice(M, min(M, 64), replace=False)
+    rows[:2] = [0, M - 1]
+    check_close(y[rows], x[rows].astype(np.float64) @ W, what=f"BT variant {layout} {K}x{N} M={M}")
+
+
 def test_no_device_error_recorded(q4):
     from aria_b200 import _lib
     assert _lib.lib().aria_q4_take_device_error() == 0
