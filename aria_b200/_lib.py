@@ -19,6 +19,7 @@ LAYOUT_KN, LAYOUT_NK = 0, 1
 FLAG_CONST_WEIGHTS = 1
 FLAG_KERNEL_STREAM = 2
 FLAG_KERNEL_REGISTER = 4
+FLAG_KERNEL_TENSOR = 8
 F32, F16 = 0, 1
 
 # every symbol include/aria_q4.h declares: (restype, argtypes)
@@ -36,6 +37,8 @@ SIGNATURES = {
     "aria_q4_0_quantize_tiled": (_I, [_P, _I, _I, _I, _P, _SZ, _P]),
     "aria_q4_0_matmul": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _F, _F, _P]),
     "aria_q4_0_matmul_ex": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _F, _F, _I, _P]),
+    "aria_q4_0_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "aria_q4_0_matmul_ws": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _F, _F, _P, _SZ, _I, _P]),
     "aria_q4_strerror": (ctypes.c_char_p, [_I]),
     "aria_q4_last_cuda_error": (_I, []),
     "aria_q4_take_device_error": (_I, []),

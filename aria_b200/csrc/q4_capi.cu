@@ -21,7 +21,9 @@ cudaError_t launch_gemv(const uint8_t* tiled, int layout, int K, int N, const __
                         int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
                         bool const_weights);
 cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
-                           int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl);
+                           int ydt, int ldy, const __half* bias, float alpha, float beta, void* workspace,
+                           size_t workspace_bytes, cudaStream_t st, bool pdl);
+size_t tc_workspace_bytes(int K, int N, int M);
 int take_device_error();
 }  // namespace aria_q4
 
@@ -128,38 +130,59 @@ int aria_q4_0_quantize_tiled(const uint16_t* w, int layout, int K, int N, void* 
   return cuda_status(launch_quantize_tiled(w, layout, K, N, (uint8_t*)tiled, (cudaStream_t)stream));
 }
 
-int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
-                        int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, int flags, void* stream) {
+size_t aria_q4_0_workspace_bytes(int K, int N, int M) {
+  if (check_tiled_shape(ARIA_Q4_LAYOUT_NK, K, N) != ARIA_Q4_OK || M <= 32) return 0;
+  return tc_workspace_bytes(K, N, M);
+}
+
+int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
+                        int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, void* workspace,
+                        size_t workspace_bytes, int flags, void* stream) {
   if (int s = check_tiled_shape(layout, K, N)) return s;
   if (M < 0) return ARIA_Q4_EINVAL;
   if (M == 0) return ARIA_Q4_OK;
   if (!tiled || !x || !y) return ARIA_Q4_EINVAL;
   if (y_dtype != ARIA_Q4_F16 && y_dtype != ARIA_Q4_F32) return ARIA_Q4_EINVAL;
   if (ldx < K || ldy < N) return ARIA_Q4_EINVAL;
-  const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_STREAM | ARIA_Q4_FLAG_KERNEL_REGISTER;
+  const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_STREAM | ARIA_Q4_FLAG_KERNEL_REGISTER |
+                    ARIA_Q4_FLAG_KERNEL_TENSOR;
   if ((flags & ~known) != 0) return ARIA_Q4_EINVAL;
   const bool want_stream = (flags & ARIA_Q4_FLAG_KERNEL_STREAM) != 0;
   const bool want_register = (flags & ARIA_Q4_FLAG_KERNEL_REGISTER) != 0;
-  if (want_stream && want_register) return ARIA_Q4_EINVAL;
+  const bool want_tensor = (flags & ARIA_Q4_FLAG_KERNEL_TENSOR) != 0;
+  if ((int)want_stream + (int)want_register + (int)want_tensor > 1) return ARIA_Q4_EINVAL;
   if (((uintptr_t)tiled & 255u) != 0 || !aligned16(x) || (ldx % 8) != 0) return ARIA_Q4_EALIGN;
+  if (workspace_bytes == 0) workspace = nullptr;
+  if (workspace && ((uintptr_t)workspace & 255u) != 0) return ARIA_Q4_EALIGN;
   if (int s = check_device()) return s;
   const cudaStream_t st = (cudaStream_t)stream;
   // Kernel choice: the streaming GEMV for M <= 8 and large weights; the
-  // register-fed decode kernel up to 32 tokens (and up to 64 when the output has
-  // too few 128-row tiles to fill the GPU with tcgen05 work); the tcgen05
-  // kernel above that.  ARIA_Q4_FLAG_KERNEL_* overrides the first two.
+  // register-fed decode kernel up to 32 tokens; the tcgen05 kernel above that
+  // (splitting K through the workspace when tiles are few).
+  // ARIA_Q4_FLAG_KERNEL_* overrides the choice.
   const bool cw = (flags & ARIA_Q4_FLAG_CONST_WEIGHTS) != 0;
   if (want_stream && !gemv_supported(K, N, M)) return ARIA_Q4_EUNSUPPORTED;
   if (want_register && M > kDecodeMaxM) return ARIA_Q4_EUNSUPPORTED;
-  if (want_stream || (!want_register && stream_by_default(K, N, M)))
+  if (want_stream || (!want_register && !want_tensor && stream_by_default(K, N, M)))
     return cuda_status(launch_gemv((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
                                    (const __half*)bias, alpha, beta, st, true, cw));
-  const bool decode = want_register || M <= 32 || (M <= kDecodeMaxM && N < 8192);
+  // Above 32 tokens the tcgen05 kernel, except without a workspace for shapes
+  // whose few output tiles it would have split over K (the register-fed kernel
+  // splits K itself).
+  const bool decode = want_register ||
+                      (!want_tensor && (M <= 32 || (M <= kDecodeMaxM && workspace == nullptr &&
+                                                    tc_workspace_bytes(K, N, M) > 0)));
   if (decode)
     return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
                                      (const __half*)bias, alpha, beta, st, true, cw));
   return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
-                                    (const __half*)bias, alpha, beta, st, true));
+                                    (const __half*)bias, alpha, beta, workspace, workspace_bytes, st, true));
+}
+
+int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
+                        int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, int flags, void* stream) {
+  return aria_q4_0_matmul_ws(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, nullptr, 0, flags,
+                             stream);
 }
 
 int aria_q4_0_matmul(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,

@@ -46,7 +46,22 @@ struct TcArgs {
   int ydt, ldy;
   const __half* bias;
   float alpha, beta;
+  // split-K: every output tile is computed as `splits` K-slices (work units);
+  // each unit's f32 partial goes to ws_part, and the last unit of a tile to
+  // finish (counted per tile and TMEM lane quadrant in ws_cnt, which every call
+  // leaves zero) adds the partials in slice order and writes the output.
+  int splits;
+  float* ws_part;
+  unsigned* ws_cnt;
 };
+
+// K-slice of work unit `unit` in 128-k groups: [g0, g1)
+__device__ __forceinline__ void tc_unit(const TcArgs& a, int unit, int KG, int& tile, int& split, int& g0, int& g1) {
+  tile = unit / a.splits;
+  split = unit - tile * a.splits;
+  g0 = split * KG / a.splits;
+  g1 = (split + 1) * KG / a.splits;
+}
 
 constexpr int kTcThreads = 448;  // 8 dequant + TMA + MMA + 4 epilogue warps
 constexpr int kBK = 64;        // k per pipeline stage (one 128-byte swizzle row of f16)
@@ -93,8 +108,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   using L = TcSmem<BT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // TMEM: two f32 accumulators [128 x BT] then kASlots dequantised A stages
-  // every free TMEM column holds A stages (up to 12): each dequant warpgroup's
+  // TMEM: NACC f32 accumulators [128 x BT], then kASlots dequantised A stages.
+  // Every free TMEM column holds A stages (up to 12): each dequant warpgroup's
   // sub-ring depth bounds how many stages are in flight between dequantisation
   // and MMA completion, which sets the stage rate when few tokens make each
   // MMA short (measured: 64 stages per tile at BT = 64 ran at ~600 cycles each
@@ -162,10 +177,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      const int KG = a.Kp >> 7;
       for (int j = 0; j < my_tiles && ok; j++) {
-        const int tile = blockIdx.x + j * gridDim.x;
+        int tile, split, g0, g1;
+        tc_unit(a, blockIdx.x + j * gridDim.x, KG, tile, split, g0, g1);
         const int m0 = (tile / n_tiles) * BT;
-        for (int kt = 0; kt < KT; kt++, it++) {
+        const int kt1 = min(2 * g1, KT);
+        for (int kt = 2 * g0; kt < kt1; kt++, it++) {
           const int s = it % STAGES;
           if (it >= STAGES && !tc::mbar_wait(&empty_x[s], ((it / STAGES) - 1) & 1)) {
             tc::record_error(tc::kErrTimeoutEmpty);
@@ -205,7 +223,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc::tc_fence_after();
         const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT);
-        for (int kt = 0; kt < KT; kt++) {
+        int tile, split, g0, g1;
+        tc_unit(a, blockIdx.x + j * gridDim.x, a.Kp >> 7, tile, split, g0, g1);
+        const int kt0 = 2 * g0, kt1 = min(2 * g1, KT);
+        for (int kt = kt0; kt < kt1; kt++) {
           const int w = (kt >> 1) & 1;  // warpgroup that dequantised this stage
           const int as = w ? kAPer + aslot1 : aslot0;
           const uint32_t aph = w ? aph1 : aph0;
@@ -225,7 +246,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; kk++)
             tc::umma_f16_ta(tmem_d, at + (uint32_t)(kk * 8), bdesc + (uint64_t)(kk * 2), idesc,
-                            (kt > 0 || kk > 0) ? 1u : 0u);
+                            (kt > kt0 || kk > 0) ? 1u : 0u);
           tc::umma_commit(&empty_x[xslot]);
           tc::umma_commit(&empty_a[as]);
           if (++xslot == STAGES) { xslot = 0; xph ^= 1u; }
@@ -250,16 +271,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int sw = (r >> 1) & 3;
     const size_t RB = (size_t)a.Kp >> 1;
     const int KG = a.Kp >> 7;
-    const int gpt = (KG - wg + 1) / 2;  // groups of this warpgroup per tile
-    const int total = my_tiles * gpt;
     uint8_t* qring = smem + L::kQOff + wg * kQDepth * kQSlot;
     uint8_t* sring = smem + L::kSOff + wg * kQDepth * kSSlot;
-    auto issue = [&](int seq) {
-      const int slot = seq % kQDepth;
-      if (seq < total) {
-        const int j = seq / gpt, G = wg + 2 * (seq % gpt);
-        const int tile = blockIdx.x + j * gridDim.x;
-        const int nb = (tile % n_tiles) * 128;
+    // This warpgroup's groups, in order: for each of the CTA's work units, the
+    // groups G of its K-slice with G % 2 == wg.  Two cursors walk the sequence:
+    // the copy issuer (kQDepth - 1 groups ahead) and the dequantiser.
+    struct Cursor {
+      int j, tile, g1, G;
+    };
+    auto cursor_first = [&](Cursor& c, int j) {
+      c.j = j;
+      c.G = 1 << 30;
+      for (; c.j < my_tiles; c.j++) {
+        int split, g0;
+        tc_unit(a, blockIdx.x + c.j * gridDim.x, KG, c.tile, split, g0, c.g1);
+        c.G = g0 + ((g0 & 1) != wg ? 1 : 0);
+        if (c.G < c.g1) return;
+      }
+    };
+    auto cursor_next = [&](Cursor& c) {
+      c.G += 2;
+      if (c.G >= c.g1) cursor_first(c, c.j + 1);
+    };
+    Cursor ic;
+    cursor_first(ic, 0);
+    int iseq = 0;
+    auto issue = [&]() {
+      const int slot = iseq % kQDepth;
+      iseq++;
+      if (ic.j < my_tiles) {
+        const int G = ic.G;
+        const int nb = (ic.tile % n_tiles) * 128;
         // codes: the warp copies its 32 rows cooperatively, lane l taking 16-byte
         // chunk l % 4 of row 8u + l / 4, so one copy instruction reads eight whole
         // 64-byte row segments (instead of 32 scattered 16-byte pieces)
@@ -283,18 +325,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const __half* ssrc = a.scales + (size_t)(ok_grp ? grp : 0) * a.Kp + (size_t)G * 128 + lane * 8;
           cp_async_16(sring + slot * kSSlot + wl * 256 + lane * 16, ssrc, ok_grp);
         }
+        cursor_next(ic);
       }
       cp_async_commit();  // an empty group keeps the wait count uniform
     };
 #pragma unroll
-    for (int p = 0; p < kQDepth - 1; p++) issue(p);
+    for (int p = 0; p < kQDepth - 1; p++) issue();
     bool ok = true;
     int seq = 0;
     int acnt = 0;  // stages this warpgroup has produced into its A sub-ring
-    for (int j = 0; j < my_tiles && ok; j++) {
-      for (int G = wg; G < KG && ok; G += 2, seq++) {
+    Cursor dc;
+    for (cursor_first(dc, 0); dc.j < my_tiles && ok; cursor_next(dc), seq++) {
+      const int G = dc.G;
+      {
         __syncwarp();  // every lane is done reading the slot the next issue overwrites
-        issue(seq + kQDepth - 1);
+        issue();
         cp_async_wait<kQDepth - 1>();  // group `seq` has landed for this thread
         __syncwarp();                  // ... and for the warp's shared KN scale row
         const int slot = seq % kQDepth;
@@ -359,10 +404,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------------------------------------ epilogue (warps 10..13)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int rr = q * 32 + lane;
+    const int KG = a.Kp >> 7;
+    // one output value: alpha * acc + bias (+ beta * y), f16 or f32
+    auto store = [&](int tok, int n, float acc, float bias) {
+      float o = fmaf(a.alpha, acc, bias);
+      const size_t idx = (size_t)tok * a.ldy + n;
+      if (a.ydt == 0) {
+        float* yp = reinterpret_cast<float*>(a.y) + idx;
+        if (a.beta != 0.0f) o += a.beta * *yp;
+        *yp = o;
+      } else {
+        __half* yp = reinterpret_cast<__half*>(a.y) + idx;
+        if (a.beta != 0.0f) o += a.beta * __half2float(*yp);
+        *yp = __float2half_rn(o);
+      }
+    };
     for (int j = 0; j < my_tiles; j++) {
       const int buf = NACC == 2 ? (j & 1) : 0;
       const int use = NACC == 2 ? (j >> 1) : j;
-      const int tile = blockIdx.x + j * gridDim.x;
+      int tile, split, g0, g1;
+      tc_unit(a, blockIdx.x + j * gridDim.x, KG, tile, split, g0, g1);
       const int n = (tile % n_tiles) * 128 + rr;
       const int m0 = (tile / n_tiles) * BT;
       // warp-uniform decisions: the per-warp arrival below is reached by all lanes or none
@@ -375,45 +436,85 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool row_ok = n < a.N;
       const float bias = (a.bias && row_ok) ? __half2float(a.bias[n]) : 0.0f;
       const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT) + ((uint32_t)(q * 32) << 16);
+      if (a.splits == 1) {
 #pragma unroll 1
-      for (int cc = 0; cc < BT / 32; cc++) {
-        uint32_t v[32];
-        tc::tmem_ld_32x32b_x32(tmem_d + (uint32_t)(cc * 32), v);
-        tc::tmem_ld_wait();
-        const int tok0 = m0 + cc * 32;
-        if (!row_ok || tok0 >= a.M) continue;
-        const int ntok = min(32, a.M - tok0);
-        if (a.ydt == 1 && a.beta == 0.0f) {  // f16 out, no accumulate: the common path
-          __half* yp = reinterpret_cast<__half*>(a.y) + (size_t)tok0 * a.ldy + n;
-          if (ntok == 32) {
+        for (int cc = 0; cc < BT / 32; cc++) {
+          uint32_t v[32];
+          tc::tmem_ld_32x32b_x32(tmem_d + (uint32_t)(cc * 32), v);
+          tc::tmem_ld_wait();
+          const int tok0 = m0 + cc * 32;
+          if (!row_ok || tok0 >= a.M) continue;
+          const int ntok = min(32, a.M - tok0);
+          if (a.ydt == 1 && a.beta == 0.0f) {  // f16 out, no accumulate: the common path
+            __half* yp = reinterpret_cast<__half*>(a.y) + (size_t)tok0 * a.ldy + n;
+            if (ntok == 32) {
 #pragma unroll
-            for (int jj = 0; jj < 32; jj++) yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
+              for (int jj = 0; jj < 32; jj++)
+                yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 32; jj++)
+                if (jj < ntok) yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
+            }
           } else {
 #pragma unroll
-            for (int jj = 0; jj < 32; jj++)
-              if (jj < ntok) yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
-          }
-        } else {
-#pragma unroll
-          for (int jj = 0; jj < 32; jj++) {
-            if (jj >= ntok) break;
-            float o = fmaf(a.alpha, __uint_as_float(v[jj]), bias);
-            const size_t idx = (size_t)(tok0 + jj) * a.ldy + n;
-            if (a.ydt == 0) {
-              float* yp = reinterpret_cast<float*>(a.y) + idx;
-              if (a.beta != 0.0f) o += a.beta * *yp;
-              *yp = o;
-            } else {
-              __half* yp = reinterpret_cast<__half*>(a.y) + idx;
-              if (a.beta != 0.0f) o += a.beta * __half2float(*yp);
-              *yp = __float2half_rn(o);
+            for (int jj = 0; jj < 32; jj++) {
+              if (jj >= ntok) break;
+              store(tok0 + jj, n, __uint_as_float(v[jj]), bias);
             }
           }
         }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
+      } else {
+        // split-K: this unit's partial [BT tokens][128 rows] f32 to the workspace
+        float* part = a.ws_part + (size_t)(tile * a.splits + split) * (128 * BT);
+#pragma unroll 1
+        for (int cc = 0; cc < BT / 32; cc++) {
+          uint32_t v[32];
+          tc::tmem_ld_32x32b_x32(tmem_d + (uint32_t)(cc * 32), v);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 32; jj++) part[(size_t)(cc * 32 + jj) * 128 + rr] = __uint_as_float(v[jj]);
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);  // the accumulator is free again
+        // publish, then count: the unit that completes a tile's quadrant adds the
+        // tile's partials in slice order (no waiting on other CTAs)
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(&a.ws_cnt[tile * 4 + q], 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == (unsigned)(a.splits - 1)) {
+          __threadfence();
+          const float* p0 = a.ws_part + (size_t)tile * a.splits * (128 * BT) + rr;
+          if (row_ok) {
+            // eight tokens at a time, every slice's partials loaded before the
+            // first add (up to 64 independent L2 loads in flight per lane)
+            for (int t0 = 0; t0 < BT && m0 + t0 < a.M; t0 += 8) {
+              float v[8][8];
+#pragma unroll
+              for (int sp = 0; sp < 8; sp++)
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                  v[sp][u] = sp < a.splits ? __ldcg(p0 + (size_t)sp * (128 * BT) + (size_t)(t0 + u) * 128) : 0.0f;
+#pragma unroll
+              for (int u = 0; u < 8; u++) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int sp = 0; sp < 8; sp++)
+                  if (sp < a.splits) acc += v[sp][u];
+                if (m0 + t0 + u < a.M) store(m0 + t0 + u, n, acc, bias);
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) a.ws_cnt[tile * 4 + q] = 0u;  // leave the counter for the next call
+        }
       }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
     }
   }
 
@@ -472,7 +573,7 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
     if (num_sms <= 0) num_sms = 148;
   }
   const int n_tiles = (a.N + 127) / 128;
-  const int num_tiles = n_tiles * ((a.M + BT - 1) / BT);
+  const int num_tiles = n_tiles * ((a.M + BT - 1) / BT) * a.splits;  // work units
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_tiles < num_sms ? num_tiles : num_sms);
   cfg.blockDim = dim3(kTcThreads);
@@ -486,19 +587,7 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
   return cudaLaunchKernelEx(&cfg, kern, tm, a, n_tiles, num_tiles);
 }
 
-// Prefill-regime projection (M > 32).  BT (tokens per CTA) follows M.
-cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
-                           int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl) {
-  TcArgs a;
-  a.qs = tiled;
-  a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
-  a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;
-  a.y = y; a.ydt = ydt; a.ldy = ldy; a.bias = bias; a.alpha = alpha; a.beta = beta;
-  // Token-tile height BT by a cost model: rounds of CTAs (tiles / SMs, rounded
-  // up) x 64-k stages per tile x (fixed issue cost of a stage + 2 cycles per
-  // token), plus, for a single accumulator, the exposed epilogue of every round
-  // after the first.  The fixed ~450 cycles per stage is the MMA issuer's
-  // latency (two barrier waits, a fence, four MMAs and two commits).
+static int tc_num_sms() {
   static int num_sms = 0;
   if (num_sms == 0) {
     int dev = 0;
@@ -506,24 +595,95 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
     cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (num_sms <= 0) num_sms = 148;
   }
+  return num_sms;
+}
+
+struct TcPlan {
+  int bt = 64, splits = 1;
+  size_t ws_bytes = 0;  // workspace the plan needs (0 without split-K)
+};
+
+// Workspace layout: a fixed counter region first (one counter per tile and TMEM
+// lane quadrant; at most kTcMaxSplitTiles tiles), then the f32 partials.  The
+// counters sit at the same place for every shape and every call returns the
+// ones it used to zero, so one workspace serves any sequence of shapes (the
+// partials region is always written before it is read).
+constexpr int kTcMaxSplitTiles = 1024;
+constexpr size_t kTcCounterBytes = (size_t)kTcMaxSplitTiles * 4 * sizeof(unsigned);
+
+static size_t tc_ws_bytes(int N, int M, int bt, int splits) {
+  if (splits <= 1) return 0;
+  const size_t tiles = (size_t)((N + 127) / 128) * ((M + bt - 1) / bt);
+  return kTcCounterBytes + tiles * splits * 128 * bt * sizeof(float);
+}
+
+// Token-tile height BT and K split by a cost model: rounds of CTAs (work units
+// / SMs, rounded up) x 64-k stages per unit x (fixed issue cost of a stage + 2
+// cycles per token), plus, for a single accumulator, the exposed epilogue of
+// every round after the first, plus, for a K split, each unit's partial write
+// and the last unit's reduction (measured: 7-9 us per round at 64 tokens, fit
+// as 10000 + 16 * S * BT in the same units).  The fixed ~450 cycles per stage is the MMA
+// issuer's latency (two barrier waits, a fence, four MMAs and two commits).  K
+// splits are considered for 64- and 128-token tiles, with every slice at least
+// two 128-k groups, when the workspace holds the plan's ws_bytes.
+static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
   struct Cand { int bt, nacc; };
   const Cand cands[] = {{64, 2}, {128, 2}, {192, 2}, {224, 1}, {256, 1}};
+  const int splits_c[] = {1, 2, 3, 4, 6, 8};  // the reduction unrolls up to 8 slices
   const long long n_tiles = (N + 127) / 128;
+  const int KG = padded_k(K) / 128;
   const long long KT = (K + kBK - 1) / kBK;
-  int best_bt = 64;
-  long long best = -1;
+  TcPlan best;
+  long long best_cost = -1;
   for (const Cand& c : cands) {
     if (c.bt > 64 && M <= 64) break;
     const long long tiles = n_tiles * ((M + c.bt - 1) / c.bt);
-    const long long rounds = (tiles + num_sms - 1) / num_sms;
-    const long long cost = rounds * KT * (450 + 2 * c.bt) + (c.nacc == 1 ? (rounds - 1) * 8 * c.bt : 0);
-    if (best < 0 || cost < best) {
-      best = cost;
-      best_bt = c.bt;
+    for (int S : splits_c) {
+      if (S > 1 && (c.bt > 128 || 2 * S > KG || tiles > kTcMaxSplitTiles)) continue;
+      const size_t need = tc_ws_bytes(N, M, c.bt, S);
+      if (S > 1 && need > ws_avail) continue;
+      const long long units = tiles * S;
+      const long long rounds = (units + sms - 1) / sms;
+      const long long stages = (KT + S - 1) / S;
+      long long cost = rounds * stages * (450 + 2 * c.bt);
+      if (c.nacc == 1) cost += (rounds - 1) * 8 * c.bt;
+      if (S > 1) cost += rounds * (10000 + 16LL * S * c.bt);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best.bt = c.bt;
+        best.splits = S;
+        best.ws_bytes = need;
+      }
     }
   }
+  return best;
+}
+
+size_t tc_workspace_bytes(int K, int N, int M) {
+  return plan_tc(K, N, M, tc_num_sms(), (size_t)-1).ws_bytes;
+}
+
+// Tensor-core projection (prefill, and batched decode above 32 tokens).
+// workspace: optional (nullptr / 0 bytes: no K split); its counter region must
+// be zero before the first use and every call leaves it zero.
+cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
+                           int ydt, int ldy, const __half* bias, float alpha, float beta, void* workspace,
+                           size_t workspace_bytes, cudaStream_t st, bool pdl) {
+  TcArgs a;
+  a.qs = tiled;
+  a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
+  a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;
+  a.y = y; a.ydt = ydt; a.ldy = ldy; a.bias = bias; a.alpha = alpha; a.beta = beta;
+  const TcPlan p = plan_tc(K, N, M, tc_num_sms(), workspace ? workspace_bytes : 0);
+  a.splits = p.splits;
+  a.ws_part = nullptr;
+  a.ws_cnt = nullptr;
+  if (p.splits > 1) {
+    a.ws_cnt = reinterpret_cast<unsigned*>(workspace);
+    a.ws_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kTcCounterBytes);
+  }
   if (layout == 1) {
-    switch (best_bt) {
+    switch (p.bt) {
       case 64: return launch_tc_t<1, 64, 8, 2>(a, x, ldx, st, pdl);
       case 128: return launch_tc_t<1, 128, 8, 2>(a, x, ldx, st, pdl);
       case 192: return launch_tc_t<1, 192, 4, 2>(a, x, ldx, st, pdl);
@@ -531,7 +691,7 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
       default: return launch_tc_t<1, 256, 4, 1>(a, x, ldx, st, pdl);
     }
   }
-  switch (best_bt) {
+  switch (p.bt) {
     case 64: return launch_tc_t<0, 64, 8, 2>(a, x, ldx, st, pdl);
     case 128: return launch_tc_t<0, 128, 8, 2>(a, x, ldx, st, pdl);
     case 192: return launch_tc_t<0, 192, 4, 2>(a, x, ldx, st, pdl);

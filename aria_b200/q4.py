@@ -128,18 +128,41 @@ class Q4Weight:
         return q
 
 
-_KERNEL_FLAGS = {"auto": 0, "stream": _lib.FLAG_KERNEL_STREAM, "register": _lib.FLAG_KERNEL_REGISTER}
+_KERNEL_FLAGS = {"auto": 0, "stream": _lib.FLAG_KERNEL_STREAM, "register": _lib.FLAG_KERNEL_REGISTER,
+                 "tensor": _lib.FLAG_KERNEL_TENSOR}
+
+
+_WORKSPACES: dict = {}
+
+
+def workspace_for(K: int, N: int, M: int, device: torch.device) -> torch.Tensor | None:
+    """Zero-filled device workspace for aria_q4_0_matmul_ws on `device` and the
+    current stream (one per pair, grown on demand; every call leaves its
+    counters zero, so it is reused as is).  None when no K split would help."""
+    nbytes = int(_lib.lib().aria_q4_0_workspace_bytes(K, N, M))
+    if nbytes == 0:
+        return None
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(device).cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 2 * (ws.numel() if ws is not None else 0)), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
 
 
 def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bias: torch.Tensor | None = None,
            alpha: float = 1.0, beta: float = 0.0, out_dtype: torch.dtype = torch.float16,
-           const_weights: bool = False, kernel: str = "auto") -> torch.Tensor:
+           const_weights: bool = False, kernel: str = "auto", workspace="auto") -> torch.Tensor:
     """y[M, N] = alpha * x[M, K] @ W + beta * out + bias, through aria_q4_0_matmul_ex.
 
     const_weights: the weight buffer is not written by the kernel preceding this
     call on the stream (model weights), so the kernel may start reading it early.
-    kernel: "auto" (the library chooses), "stream" (streaming GEMV, M <= 8) or
-    "register" (register-fed decode kernel, M <= 64)."""
+    kernel: "auto" (the library chooses), "stream" (streaming GEMV, M <= 8),
+    "register" (register-fed decode kernel, M <= 64) or "tensor" (tcgen05 kernel).
+    workspace: "auto" (a cached per-device/stream buffer sized by
+    aria_q4_0_workspace_bytes), None (no K split) or a zero-initialised uint8
+    CUDA tensor owned by the caller."""
     _require_cuda(x, "x")
     if x.dtype != torch.float16:
         raise TypeError("x must be f16 (the reference's activation dtype)")
@@ -157,9 +180,17 @@ def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bia
         _require_cuda(bias, "bias")
         if bias.dtype != torch.float16 or bias.numel() != w.N:
             raise ValueError("bias must be f16 [N]")
-    call("aria_q4_0_matmul_ex", w.buf.data_ptr(), w.layout, w.K, w.N, x2.data_ptr(), M, x2.stride(0),
+    if isinstance(workspace, str):
+        if workspace != "auto":
+            raise ValueError("workspace must be 'auto', None or a uint8 CUDA tensor")
+        workspace = workspace_for(w.K, w.N, M, x.device) if M > 32 else None
+    if workspace is not None:
+        _require_cuda(workspace, "workspace")
+    call("aria_q4_0_matmul_ws", w.buf.data_ptr(), w.layout, w.K, w.N, x2.data_ptr(), M, x2.stride(0),
          out.data_ptr(), ydt, out.reshape(-1, w.N).stride(0),
          bias.data_ptr() if bias is not None else None, float(alpha), float(beta),
+         workspace.data_ptr() if workspace is not None else None,
+         workspace.numel() * workspace.element_size() if workspace is not None else 0,
          (_lib.FLAG_CONST_WEIGHTS if const_weights else 0) | _KERNEL_FLAGS[kernel], _stream(x.device))
     return out
 

@@ -115,13 +115,15 @@ enum {
    * weight streaming with the previous projection's tail.  Leave it clear when
    * the weights were just produced on the same stream (repack/quantize). */
   ARIA_Q4_FLAG_CONST_WEIGHTS = 1,
-  /* Kernel selection (at most one; without either the library chooses).
+  /* Kernel selection (at most one; without any the library chooses).
    * STREAM: the streaming GEMV (M <= 8; each warp streams packed chunks through a
    * shared-memory ring; best for weights of tens of MB).  REGISTER: the
    * register-fed decode kernel (M <= 64; lowest latency for small weights).
    * ARIA_Q4_EUNSUPPORTED when the chosen kernel cannot take the shape. */
   ARIA_Q4_FLAG_KERNEL_STREAM = 2,
-  ARIA_Q4_FLAG_KERNEL_REGISTER = 4
+  ARIA_Q4_FLAG_KERNEL_REGISTER = 4,
+  /* TENSOR: the tcgen05 tensor-core kernel (any M >= 1). */
+  ARIA_Q4_FLAG_KERNEL_TENSOR = 8
 };
 
 /* aria_q4_0_matmul with scheduling flags (ARIA_Q4_FLAG_*); flags = 0 is exactly
@@ -131,6 +133,24 @@ ARIA_Q4_API int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N,
                         const uint16_t* x, int M, int ldx,
                         void* y, int y_dtype, int ldy,
                         const uint16_t* bias, float alpha, float beta, int flags, void* stream);
+
+/* Bytes of workspace with which aria_q4_0_matmul_ws may split K for this
+ * shape (0: no split would help).  The workspace proposed for the reference's
+ * gemm() replacement (`void* workspace, size_t ws_bytes`). */
+ARIA_Q4_API size_t aria_q4_0_workspace_bytes(int K, int N, int M);
+
+/* aria_q4_0_matmul_ex with a caller-owned device workspace (256-byte aligned;
+ * NULL or 0 bytes: no K split).  When the tensor-core kernel has fewer output
+ * tiles than SMs it splits K into work units whose f32 partials go to the
+ * workspace; the last unit of each tile adds them in slice order (results are
+ * reproducible).  The workspace must be zero-filled before its first use;
+ * every call, of any shape, leaves it ready for the next.  Calls that share a
+ * workspace must be ordered (one stream, or events). */
+ARIA_Q4_API int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N,
+                        const uint16_t* x, int M, int ldx,
+                        void* y, int y_dtype, int ldy,
+                        const uint16_t* bias, float alpha, float beta,
+                        void* workspace, size_t workspace_bytes, int flags, void* stream);
 
 /* ---------------------------------------------------------------- errors */
 

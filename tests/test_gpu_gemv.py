@@ -106,7 +106,9 @@ def test_kernel_flags_errors(q4):
     def rc(M, flags):
         return L.aria_q4_0_matmul_ex(w.buf.data_ptr(), 0, 64, 64, x.data_ptr(), M, 64, y.data_ptr(), 1, 64, None,
                                      1.0, 0.0, flags, None)
-    assert rc(1, 2 | 4) == 1   # both kernels requested: EINVAL
+    assert rc(1, 2 | 4) == 1   # two kernels requested: EINVAL
+    assert rc(1, 4 | 8) == 1
+    assert rc(1, 8) == 0       # the tcgen05 kernel takes any M
     assert rc(9, 2) == 2       # streaming GEMV takes M <= 8: EUNSUPPORTED
     assert rc(65, 4) == 2      # register-fed kernel takes M <= 64: EUNSUPPORTED
     assert rc(8, 2) == 0 and rc(64, 4) == 0

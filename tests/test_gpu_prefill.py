@@ -29,12 +29,12 @@ def _weights(coracle, layout, K, N, seed, sigma=0.02):
     return w, blocks, W
 
 
-def _run(q4, w, layout, x, out_dtype=torch.float16, bias=None, alpha=1.0, beta=0.0, y0=None):
+def _run(q4, w, layout, x, out_dtype=torch.float16, bias=None, alpha=1.0, beta=0.0, y0=None, kernel="auto"):
     wq = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
     xt = torch.from_numpy(x).cuda()
     out = torch.from_numpy(y0).to(out_dtype).cuda() if y0 is not None else None
     bt = torch.from_numpy(bias).cuda() if bias is not None else None
-    y = q4.matmul(xt, wq, out, bias=bt, alpha=alpha, beta=beta, out_dtype=out_dtype)
+    y = q4.matmul(xt, wq, out, bias=bt, alpha=alpha, beta=beta, out_dtype=out_dtype, kernel=kernel)
     torch.cuda.synchronize()
     return y.cpu().to(torch.float64).numpy()
 
@@ -104,6 +104,60 @@ def test_prefill_token_tile_variants(q4, coracle, layout, K, N, M):
     rows = np.random.default_rng(5).choice(M, min(M, 64), replace=False)
     rows[:2] = [0, M - 1]
     check_close(y[rows], x[rows].astype(np.float64) @ W, what=f"BT variant {layout} {K}x{N} M={M}")
+
+
+@pytest.mark.parametrize("M", [1, 8, 33, 64])
+@pytest.mark.parametrize("layout,K,N", [(LAYOUT_KN, 896, 2688), (LAYOUT_NK, 1056, 300)])
+def test_tensor_kernel_small_m(q4, coracle, layout, K, N, M):
+    """ARIA_Q4_FLAG_KERNEL_TENSOR: the tcgen05 kernel at decode-sized M (token
+    rows past M are zero-filled by the tensor map and never stored)."""
+    w, blocks, W = _weights(coracle, layout, K, N, seed=M + 17)
+    x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float16)
+    b = (np.random.default_rng(M + 1).standard_normal(N) * 0.1).astype(np.float16)
+    y = _run(q4, w, layout, x, bias=b, kernel="tensor")
+    check_close(y, x.astype(np.float64) @ W + b.astype(np.float64), what=f"tensor M={M}")
+
+
+@pytest.mark.parametrize("layout,K,N,M", [
+    (LAYOUT_KN, 16384, 512, 64),    # 4 row tiles, 128 groups of k: deep K split
+    (LAYOUT_NK, 3584, 896, 64),     # the Efkolos ffn_down shape at batch 64
+    (LAYOUT_KN, 3584, 896, 40),
+    (LAYOUT_NK, 4096, 300, 100),    # ragged N, 128-token tiles
+    (LAYOUT_KN, 8224, 256, 50),     # K % 128 != 0: the last slice holds the padded tail
+])
+def test_split_k_through_workspace(q4, coracle, layout, K, N, M):
+    """aria_q4_0_matmul_ws: few output tiles, long K -> work units over K
+    slices, partials in the workspace, the last unit of each tile adds them in
+    slice order.  Two calls in a row (the second relies on the first leaving its
+    counters at zero) give identical bits; both are within tolerance of fp64."""
+    from aria_b200 import _lib
+    assert _lib.lib().aria_q4_0_workspace_bytes(K, N, M) > 0, "shape should split K"
+    w, blocks, W = _weights(coracle, layout, K, N, seed=K + N + 5 * M)
+    x = np.random.default_rng(M + 7).standard_normal((M, K)).astype(np.float16)
+    b = (np.random.default_rng(M + 8).standard_normal(N) * 0.1).astype(np.float16)
+    wq = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
+    xt, bt = torch.from_numpy(x).cuda(), torch.from_numpy(b).cuda()
+    ws = torch.zeros(int(_lib.lib().aria_q4_0_workspace_bytes(K, N, M)), dtype=torch.uint8, device="cuda")
+    y1 = q4.matmul(xt, wq, bias=bt, out_dtype=torch.float32, kernel="tensor", workspace=ws)
+    y2 = q4.matmul(xt, wq, bias=bt, out_dtype=torch.float32, kernel="tensor", workspace=ws)
+    y0 = q4.matmul(xt, wq, bias=bt, out_dtype=torch.float32, kernel="tensor", workspace=None)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    ref = x.astype(np.float64) @ W + b.astype(np.float64)
+    check_close(y1.cpu().numpy(), ref, what=f"split-K {layout} {K}x{N} M={M}")
+    check_close(y0.cpu().numpy(), ref, what=f"unsplit {layout} {K}x{N} M={M}")
+
+
+def test_one_workspace_serves_any_shape_sequence(q4, coracle):
+    """Auto workspace (one cached buffer per device and stream) across shapes
+    with different tile counts and splits, in both orders."""
+    shapes = [(LAYOUT_KN, 896, 2688, 40), (LAYOUT_KN, 896, 896, 33), (LAYOUT_KN, 16384, 512, 64),
+              (LAYOUT_NK, 3584, 896, 64), (LAYOUT_KN, 896, 896, 33), (LAYOUT_KN, 896, 2688, 40)]
+    for layout, K, N, M in shapes:
+        w, blocks, W = _weights(coracle, layout, K, N, seed=N + M)
+        x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float16)
+        y = _run(q4, w, layout, x, out_dtype=torch.float32)
+        check_close(y, x.astype(np.float64) @ W, what=f"sequence {layout} {K}x{N} M={M}")
 
 
 def test_no_device_error_recorded(q4):

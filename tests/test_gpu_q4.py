@@ -179,5 +179,5 @@ def test_matmul_ex_rejects_unknown_flags(q4):
     x = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
     y = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
     rc = lib().aria_q4_0_matmul_ex(w.buf.data_ptr(), 0, 64, 64, x.data_ptr(), 1, 64, y.data_ptr(), 1, 64, None,
-                                   1.0, 0.0, 8, None)
+                                   1.0, 0.0, 16, None)
     assert rc == 1
