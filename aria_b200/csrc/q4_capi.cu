@@ -24,6 +24,7 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
                            int ydt, int ldy, const __half* bias, float alpha, float beta, void* workspace,
                            size_t workspace_bytes, cudaStream_t st, bool pdl);
 size_t tc_workspace_bytes(int K, int N, int M);
+size_t tc_workspace_counter_bytes();
 int take_device_error();
 }  // namespace aria_q4
 
@@ -182,6 +183,55 @@ int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint1
 int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
                         int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, int flags, void* stream) {
   return aria_q4_0_matmul_ws(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, nullptr, 0, flags,
+                             stream);
+}
+
+// ------------------------------------------------------------------ static-scratch variant
+// Scratch of aria_q4_0_matmul_static_ws: one file-scope device array per
+// device (zero at module load), so the call allocates nothing.
+static constexpr size_t kStaticWsBytes = 8u << 20;
+static __device__ __align__(256) unsigned char g_static_ws[kStaticWsBytes];
+
+// Device address of g_static_ws on the current device, looked up once per
+// device; nullptr (and *err set) when the lookup fails.
+static void* static_ws_address(cudaError_t* err) {
+  constexpr int kMaxDevices = 64;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess && (dev < 0 || dev >= kMaxDevices)) e = cudaErrorInvalidDevice;
+  if (e != cudaSuccess) {
+    *err = e;
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_ws);
+    if (e != cudaSuccess) {
+      *err = e;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx,
+                               void* y, int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta,
+                               int flags, void* stream) {
+  // the workspace the tensor-core kernel's plan would use (only M > 32 splits K)
+  const size_t need = (M > 32 && check_tiled_shape(layout, K, N) == ARIA_Q4_OK) ? tc_workspace_bytes(K, N, M) : 0;
+  if (need > kStaticWsBytes) return ARIA_Q4_ESIZE;
+  void* ws = nullptr;
+  if (need > 0) {
+    cudaError_t e = cudaSuccess;
+    ws = static_ws_address(&e);
+    if (!ws) return cuda_status(e);
+    // the split-K counters must start at zero (a call cut short may leave them set)
+    e = cudaMemsetAsync(ws, 0, tc_workspace_counter_bytes(), (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return aria_q4_0_matmul_ws(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, ws, need, flags,
                              stream);
 }
 

@@ -663,6 +663,9 @@ size_t tc_workspace_bytes(int K, int N, int M) {
   return plan_tc(K, N, M, tc_num_sms(), (size_t)-1).ws_bytes;
 }
 
+// Bytes at the start of a workspace that hold the split-K counters.
+size_t tc_workspace_counter_bytes() { return kTcCounterBytes; }
+
 // Tensor-core projection (prefill, and batched decode above 32 tokens).
 // workspace: optional (nullptr / 0 bytes: no K split); its counter region must
 // be zero before the first use and every call leaves it zero.

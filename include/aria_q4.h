@@ -152,6 +152,18 @@ ARIA_Q4_API int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N,
                         const uint16_t* bias, float alpha, float beta,
                         void* workspace, size_t workspace_bytes, int flags, void* stream);
 
+/* aria_q4_0_matmul_ex that allocates nothing: when the tensor-core kernel would
+ * split K it uses the library's own static device scratch (8 MiB per device)
+ * instead of a caller workspace, first clearing its counter region on the
+ * stream; ARIA_Q4_ESIZE when the split needs more than that.  Every call on a
+ * device shares that one scratch: calls that overlap in time (unordered
+ * streams, or several host threads) corrupt each other's partial sums, so
+ * order them on one stream.  No counterpart in the reference. */
+ARIA_Q4_API int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K, int N,
+                        const uint16_t* x, int M, int ldx,
+                        void* y, int y_dtype, int ldy,
+                        const uint16_t* bias, float alpha, float beta, int flags, void* stream);
+
 /* ---------------------------------------------------------------- errors */
 
 ARIA_Q4_API const char* aria_q4_strerror(int status);
