@@ -131,6 +131,26 @@ int aria_q4_0_quantize_tiled(const uint16_t* w, int layout, int K, int N, void* 
   return cuda_status(launch_quantize_tiled(w, layout, K, N, (uint8_t*)tiled, (cudaStream_t)stream));
 }
 
+// Kernel choice: the streaming GEMV for M <= 8 and large weights; the
+// register-fed decode kernel up to 32 tokens; the tcgen05 kernel above that
+// (splitting K through the workspace when tiles are few), except without a
+// workspace for the shapes it would have split (the register-fed kernel splits
+// K itself, up to 64 tokens).  ARIA_Q4_FLAG_KERNEL_* overrides the choice.
+// Returns an ARIA_Q4_KERNEL_* value, or a negated status.
+static int choose_kernel(int K, int N, int M, bool has_workspace, int flags) {
+  const bool want_stream = (flags & ARIA_Q4_FLAG_KERNEL_STREAM) != 0;
+  const bool want_register = (flags & ARIA_Q4_FLAG_KERNEL_REGISTER) != 0;
+  const bool want_tensor = (flags & ARIA_Q4_FLAG_KERNEL_TENSOR) != 0;
+  if ((int)want_stream + (int)want_register + (int)want_tensor > 1) return -ARIA_Q4_EINVAL;
+  if (want_stream) return gemv_supported(K, N, M) ? ARIA_Q4_KERNEL_STREAM : -ARIA_Q4_EUNSUPPORTED;
+  if (want_register) return M <= kDecodeMaxM ? ARIA_Q4_KERNEL_REGISTER : -ARIA_Q4_EUNSUPPORTED;
+  if (want_tensor) return ARIA_Q4_KERNEL_TENSOR;
+  if (stream_by_default(K, N, M)) return ARIA_Q4_KERNEL_STREAM;
+  if (M <= 32 || (M <= kDecodeMaxM && !has_workspace && tc_workspace_bytes(K, N, M) > 0))
+    return ARIA_Q4_KERNEL_REGISTER;
+  return ARIA_Q4_KERNEL_TENSOR;
+}
+
 size_t aria_q4_0_workspace_bytes(int K, int N, int M) {
   if (check_tiled_shape(ARIA_Q4_LAYOUT_NK, K, N) != ARIA_Q4_OK || M <= 32) return 0;
   return tc_workspace_bytes(K, N, M);
@@ -148,36 +168,31 @@ int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint1
   const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_STREAM | ARIA_Q4_FLAG_KERNEL_REGISTER |
                     ARIA_Q4_FLAG_KERNEL_TENSOR;
   if ((flags & ~known) != 0) return ARIA_Q4_EINVAL;
-  const bool want_stream = (flags & ARIA_Q4_FLAG_KERNEL_STREAM) != 0;
-  const bool want_register = (flags & ARIA_Q4_FLAG_KERNEL_REGISTER) != 0;
-  const bool want_tensor = (flags & ARIA_Q4_FLAG_KERNEL_TENSOR) != 0;
-  if ((int)want_stream + (int)want_register + (int)want_tensor > 1) return ARIA_Q4_EINVAL;
   if (((uintptr_t)tiled & 255u) != 0 || !aligned16(x) || (ldx % 8) != 0) return ARIA_Q4_EALIGN;
   if (workspace_bytes == 0) workspace = nullptr;
   if (workspace && ((uintptr_t)workspace & 255u) != 0) return ARIA_Q4_EALIGN;
   if (int s = check_device()) return s;
   const cudaStream_t st = (cudaStream_t)stream;
-  // Kernel choice: the streaming GEMV for M <= 8 and large weights; the
-  // register-fed decode kernel up to 32 tokens; the tcgen05 kernel above that
-  // (splitting K through the workspace when tiles are few).
-  // ARIA_Q4_FLAG_KERNEL_* overrides the choice.
+  const int kern = choose_kernel(K, N, M, workspace != nullptr, flags);
+  if (kern < 0) return -kern;
   const bool cw = (flags & ARIA_Q4_FLAG_CONST_WEIGHTS) != 0;
-  if (want_stream && !gemv_supported(K, N, M)) return ARIA_Q4_EUNSUPPORTED;
-  if (want_register && M > kDecodeMaxM) return ARIA_Q4_EUNSUPPORTED;
-  if (want_stream || (!want_register && !want_tensor && stream_by_default(K, N, M)))
+  if (kern == ARIA_Q4_KERNEL_STREAM)
     return cuda_status(launch_gemv((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
                                    (const __half*)bias, alpha, beta, st, true, cw));
-  // Above 32 tokens the tcgen05 kernel, except without a workspace for shapes
-  // whose few output tiles it would have split over K (the register-fed kernel
-  // splits K itself).
-  const bool decode = want_register ||
-                      (!want_tensor && (M <= 32 || (M <= kDecodeMaxM && workspace == nullptr &&
-                                                    tc_workspace_bytes(K, N, M) > 0)));
-  if (decode)
+  if (kern == ARIA_Q4_KERNEL_REGISTER)
     return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
                                      (const __half*)bias, alpha, beta, st, true, cw));
   return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
                                     (const __half*)bias, alpha, beta, workspace, workspace_bytes, st, true));
+}
+
+int aria_q4_0_kernel_choice(int layout, int K, int N, int M, size_t workspace_bytes, int flags) {
+  if (int s = check_tiled_shape(layout, K, N)) return -s;
+  if (M < 1) return -ARIA_Q4_EINVAL;
+  const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_STREAM | ARIA_Q4_FLAG_KERNEL_REGISTER |
+                    ARIA_Q4_FLAG_KERNEL_TENSOR;
+  if ((flags & ~known) != 0) return -ARIA_Q4_EINVAL;
+  return choose_kernel(K, N, M, workspace_bytes != 0, flags);
 }
 
 int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,

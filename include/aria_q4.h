@@ -152,6 +152,19 @@ ARIA_Q4_API int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N,
                         const uint16_t* bias, float alpha, float beta,
                         void* workspace, size_t workspace_bytes, int flags, void* stream);
 
+/* Kernels aria_q4_0_matmul_ws can run. */
+enum {
+  ARIA_Q4_KERNEL_STREAM = 1,    /* streaming GEMV (gemv_stream_kernel) */
+  ARIA_Q4_KERNEL_REGISTER = 2,  /* register-fed decode kernel (decode_mma_kernel) */
+  ARIA_Q4_KERNEL_TENSOR = 3     /* tcgen05 kernel (gemm_tc_kernel) */
+};
+
+/* The kernel aria_q4_0_matmul_ws would launch for this shape, a workspace of
+ * workspace_bytes (0: none) and these flags; a negated status code when the
+ * arguments would be rejected.  No reference counterpart (introspection for
+ * benchmarks and tests). */
+ARIA_Q4_API int aria_q4_0_kernel_choice(int layout, int K, int N, int M, size_t workspace_bytes, int flags);
+
 /* aria_q4_0_matmul_ex that allocates nothing: when the tensor-core kernel would
  * split K it uses the library's own static device scratch (8 MiB per device)
  * instead of a caller workspace, first clearing its counter region on the

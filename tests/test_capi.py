@@ -65,3 +65,27 @@ def test_argument_errors_need_no_gpu(lib):
     assert lib.aria_q4_0_repack(P(256), 1, 64, 64, P(260), 1 << 20, None) == 3
     assert lib.aria_q4_0_pack_f16(None, 0, None, None) == 0
     assert lib.aria_q4_0_pack_f16(None, 5, None, None) == 1
+
+
+def test_kernel_choice_routing():
+    """aria_q4_0_kernel_choice (no GPU needed: the planners fall back to 148 SMs)."""
+    from aria_b200._lib import lib
+    L = lib()
+    STREAM, REGISTER, TENSOR = 1, 2, 3
+    KN, NK = 0, 1
+    assert L.aria_q4_0_kernel_choice(KN, 896, 2688, 1, 0, 0) == REGISTER    # small weight: latency-bound
+    assert L.aria_q4_0_kernel_choice(NK, 896, 31500, 1, 0, 0) == STREAM     # 15.9 MB: bandwidth-bound
+    assert L.aria_q4_0_kernel_choice(KN, 4096, 16384, 8, 0, 0) == STREAM
+    assert L.aria_q4_0_kernel_choice(KN, 896, 2688, 16, 0, 0) == REGISTER
+    assert L.aria_q4_0_kernel_choice(KN, 896, 2688, 64, 0, 0) == TENSOR     # no K split needed
+    assert L.aria_q4_0_workspace_bytes(3584, 896, 64) > 0
+    assert L.aria_q4_0_kernel_choice(NK, 3584, 896, 64, 0, 0) == REGISTER   # would split K, no workspace
+    assert L.aria_q4_0_kernel_choice(NK, 3584, 896, 64, 1 << 20, 0) == TENSOR
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 4096, 0, 0) == TENSOR
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 2) == STREAM       # forced
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 9, 0, 2) == -2           # stream takes M <= 8
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 65, 0, 4) == -2          # register takes M <= 64
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 2 | 4) == -1       # two kernels requested
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 8) == TENSOR
+    assert L.aria_q4_0_kernel_choice(KN, 896, 48, 1, 0, 0) == -2            # KN needs N % 32 == 0
+
