@@ -216,6 +216,50 @@ def scaled_section(args, rank, world, local_rank, stream, timed, peaks):
     return out
 
 
+# ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of the decode
+# step's dominant kernel kind (profiles/decode_mma_ffn_down_M1.md, one cold launch)
+NCU_TRAFFIC = {"ffn_down": 1838336}
+
+
+def kernel_name(w, M: int, workspace_bytes: int = 0) -> str:
+    """The kernel the library routes this projection to (aria_q4_0_kernel_choice)."""
+    from aria_b200._lib import lib
+    k = lib().aria_q4_0_kernel_choice(w.layout, w.K, w.N, M, workspace_bytes, 0)
+    return {1: "gemv_stream_kernel", 2: "decode_mma_kernel", 3: "gemm_tc_kernel"}.get(k, f"status {-k}")
+
+
+def gemv_config4_b1(stream, timed, l2: int, hbm_peak: float) -> dict:
+    """Each config-4 projection kind alone at M=1, launched as a chain with the
+    const-weights flag over weight copies totalling > 4x L2."""
+    import torch
+    from aria_b200.efkolos import SCALED, synth_f16
+    from aria_b200.q4 import Q4Weight, matmul
+    out = {"workload": "BASELINE configs[4] projections, one token, each kind chained over copies > 4x L2"}
+    for (name, lay, K, N, sigma) in SCALED.projections()[:4] + [SCALED.lm_head()]:
+        kind = name.split(".")[-1]
+        shape = (K, N) if lay == 0 else (N, K)
+        w0 = Q4Weight.from_f16(synth_f16(shape, sigma, 3), lay)
+        ncopy = max(4, -(-4 * l2 // w0.nbytes))
+        pool = [w0] + [Q4Weight(w0.buf.clone(), lay, K, N) for _ in range(ncopy - 1)]
+        x = synth_f16((1, K), 1.0, 4)
+        y = torch.empty(1, N, dtype=torch.float16, device=x.device)
+        n = max(32, ncopy)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            matmul(x, pool[0], y, const_weights=True)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=stream):
+                for j in range(n):
+                    matmul(x, pool[j % ncopy], y, const_weights=True)
+        us = timed(lambda i: g.replay(), 5, 3, f"aria_gemv4_{kind}") * 1e3 / (5 * n)
+        abytes = w0.nbytes + K * 2 + N * 2
+        out[kind] = {"K": K, "N": N, "kernel": kernel_name(w0, 1), "us_per_launch": round(us, 3),
+                     "GBs": abytes / (us * 1e-6) / 1e9, "frac_of_measured_hbm": abytes / (us * 1e-6) / 1e9 / hbm_peak}
+        del g, pool, w0
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
@@ -314,10 +358,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         torch.cuda.empty_cache()
     dom = max(per_kind, key=lambda k: per_kind[k]["share_est"])
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    roof = {"bound": "hbm", "kernel": f"decode_mma_kernel ({dom})", "achieved": per_kind[dom]["gbs"], "peak": hbm_peak,
-            "unit": "GB/s", "frac": per_kind[dom]["gbs"] / hbm_peak, "traffic": None,
+    wdom = stack0.weights[kinds[dom][0]][1]
+    roof = {"bound": "hbm", "kernel": f"{kernel_name(wdom, 1)} ({dom})", "achieved": per_kind[dom]["gbs"],
+            "peak": hbm_peak, "unit": "GB/s", "frac": per_kind[dom]["gbs"] / hbm_peak,
+            "traffic": NCU_TRAFFIC.get(dom), "traffic_source": "profiles/decode_mma_ffn_down_M1.md (ncu, bytes per launch)",
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
             "per_kind": per_kind}
+    for k in per_kind:
+        w_k = stack0.weights[kinds[k][0]][1]
+        per_kind[k]["kernel"] = kernel_name(w_k, 1)
+
+    # ---- the streaming GEMV on BASELINE configs[4] weights (d_model 4096) at one
+    # token: bandwidth-bound projections large enough to show the kernel's
+    # streaming rate (the Efkolos layers are latency-bound)
+    gemv_large = gemv_config4_b1(stream, timed, l2, hbm_peak)
 
     # ---- end to end through the public API with host buffers
     x_host = torch.empty_like(prog.x_all, device="cpu").pin_memory()
@@ -401,6 +455,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                        "flops_per_token": flops_token, "peak_tflops_measured": bf16_peak,
                        "peak_tflops_sustained": bf16_sus, **prefill},
            "scaled": scaled,
+           "gemv_config4_b1": gemv_large,
            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": prog.input_bytes(),
                    "d2h_bytes_per_step": prog.ys[-1].numel() * 2, "ms_per_step": e2e_ms},
            "gpu_launches": prog.launches * args.steps}
