@@ -36,14 +36,17 @@ int take_device_error();
 static const int kDecodeMaxM = ARIA_Q4_DECODE_MAX_M;
 
 // Default decode-kernel choice: the streaming GEMV for M <= 8 when the weight
-// is at least kStreamMinBytesPerSm of packed bytes per SM (below that a
+// is at least kStreamMinBytesPerSm of packed bytes per SM, or K is tall (the
+// register-fed kernel then needs clusters to split K; measured on the Efkolos
+// ffn_down, K = 3584: 4.0 against 4.4 us per chained launch).  Below that a
 // projection is latency-bound and the register-fed kernel, with its smaller
-// CTAs, overlaps better with its neighbours in a chain of projections).
+// CTAs, overlaps better with its neighbours in a chain of projections.
 static const double kStreamMinBytesPerSm = 32.0 * 1024;
+static const int kStreamMinK = 2048;
 static bool stream_by_default(int K, int N, int M) {
   if (M > 8) return false;
   const double per_sm = (double)N * (aria_q4::padded_k(K) / 128) * 72.0 / 148.0;
-  return per_sm >= kStreamMinBytesPerSm && aria_q4::gemv_supported(K, N, M);
+  return (per_sm >= kStreamMinBytesPerSm || K >= kStreamMinK) && aria_q4::gemv_supported(K, N, M);
 }
 
 using namespace aria_q4;

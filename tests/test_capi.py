@@ -77,6 +77,7 @@ def test_kernel_choice_routing():
     assert L.aria_q4_0_kernel_choice(NK, 896, 31500, 1, 0, 0) == STREAM     # 15.9 MB: bandwidth-bound
     assert L.aria_q4_0_kernel_choice(KN, 4096, 16384, 8, 0, 0) == STREAM
     assert L.aria_q4_0_kernel_choice(KN, 896, 2688, 16, 0, 0) == REGISTER
+    assert L.aria_q4_0_kernel_choice(KN, 3584, 896, 1, 0, 0) == STREAM      # tall K
     assert L.aria_q4_0_kernel_choice(KN, 896, 2688, 64, 0, 0) == TENSOR     # no K split needed
     assert L.aria_q4_0_workspace_bytes(3584, 896, 64) > 0
     assert L.aria_q4_0_kernel_choice(NK, 3584, 896, 64, 0, 0) == REGISTER   # would split K, no workspace
