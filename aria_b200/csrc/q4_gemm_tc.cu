@@ -10,9 +10,10 @@
 // tokens] = W_tile[128 x K] . X_tile[BT x K]^T ("swap AB": the weights are the
 // 128-row UMMA operand, so each dequantised weight serves BT = up to 256 tokens).
 // Fourteen warps, specialised:
-//   warp 8      TMA producer: X tiles [BT x 64 k] f16, 128-byte swizzle, no multicast
-//   warps 0-7   dequantisers, two warpgroups taking alternate 128-k groups (two 64-k
-//               stages each): one weight row per thread; the row's codes are streamed
+//   warp 8      TMA producer: X tiles [BT x 128 k] f16 per stage (two 64-k boxes,
+//               128-byte swizzle, no multicast)
+//   warps 0-7   dequantisers, two warpgroups taking alternate 128-k groups (one
+//               stage each): one weight row per thread; the row's codes are streamed
 //               with cp.async into a shared-memory ring several groups ahead, turned into (q-8)*scale f16
 //               (LOP3/HSUB/HMUL) and written with tcgen05.st straight into tensor
 //               memory, where the MMA reads its A operand: the dequantised weights
@@ -24,8 +25,10 @@
 //               hands finished accumulators to the epilogue
 //   warps 10-13 epilogue: tcgen05.ld of one of two TMEM accumulators (so the next
 //               tile's MMAs overlap this tile's stores), alpha/bias/beta, f16/f32 store
-// Operand stages are an mbarrier ring (STAGES deep); the two accumulators have
-// their own full/empty barriers.  Every wait is bounded (one second); on expiry
+// Operand stages (128 k: one code group) are an mbarrier ring (STAGES deep); the
+// accumulators have their own full/empty barriers.  A stage of 128 k rather
+// than 64 k halves the barrier waits, fences and commits the single MMA-issuing
+// thread performs per MMA -- that thread's issue latency bounds the pipe.  Every wait is bounded (one second); on expiry
 // the kernel records an error code in g_device_error, unwinds, frees its TMEM
 // and returns instead of hanging the GPU.
 //
@@ -64,8 +67,9 @@ __device__ __forceinline__ void tc_unit(const TcArgs& a, int unit, int KG, int& 
 }
 
 constexpr int kTcThreads = 448;  // 8 dequant + TMA + MMA + 4 epilogue warps
-constexpr int kBK = 64;        // k per pipeline stage (one 128-byte swizzle row of f16)
-constexpr int kAStageCols = 32;  // TMEM columns of one dequantised A stage: 128 rows x 64 k f16
+constexpr int kBK = 64;         // k per TMA box (one 128-byte swizzle row of f16)
+constexpr int kStageK = 128;    // k per pipeline stage: one 128-k code group, two TMA boxes
+constexpr int kAStageCols = 64;  // TMEM columns of one dequantised A stage: 128 rows x 128 k f16
 
 constexpr int kQDepth = 4;  // 128-k code groups in flight per dequant warpgroup
 // per warpgroup and ring slot: each row's whole 64-byte code group (128 rows) and
@@ -75,8 +79,8 @@ constexpr int kSSlot = 128 * 8 > 4 * 256 ? 128 * 8 : 4 * 256;
 
 template <int BT, int STAGES>
 struct TcSmem {
-  static constexpr int kXTile = BT * kBK * 2;
-  static constexpr int kStage = kXTile;
+  static constexpr int kXTile = BT * kBK * 2;  // one TMA box [BT x 64 k]
+  static constexpr int kStage = 2 * kXTile;     // one 128-k stage
   static constexpr int kQOff = STAGES * kStage;
   static constexpr int kSOff = kQOff + 2 * kQDepth * kQSlot;
   static constexpr int kBarOff = kSOff + 2 * kQDepth * kSSlot;
@@ -118,7 +122,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // epilogue; NACC = 1 leaves TMEM room for token tiles up to 256 (for shapes
   // whose tiles fit one round of CTAs there is no next tile to overlap).
   constexpr int kFreeCols = 512 - NACC * BT;
-  constexpr int kASlots = kFreeCols / kAStageCols >= 12 ? 12 : (kFreeCols / kAStageCols) & ~1;
+  constexpr int kASlots = kFreeCols / kAStageCols >= 8 ? 8 : (kFreeCols / kAStageCols) & ~1;
   static_assert(kASlots >= 4, "two A slots per dequant warpgroup");
   constexpr int kAPer = kASlots / 2;
   constexpr uint32_t kAColBase = NACC * BT;  // A stages follow the accumulators
@@ -140,7 +144,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = (a.K + kBK - 1) / kBK;
   const int my_tiles = (num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
   if (threadIdx.x == 0) {
@@ -182,16 +185,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int tile, split, g0, g1;
         tc_unit(a, blockIdx.x + j * gridDim.x, KG, tile, split, g0, g1);
         const int m0 = (tile / n_tiles) * BT;
-        const int kt1 = min(2 * g1, KT);
-        for (int kt = 2 * g0; kt < kt1; kt++, it++) {
+        for (int G = g0; G < g1; G++, it++) {
           const int s = it % STAGES;
           if (it >= STAGES && !tc::mbar_wait(&empty_x[s], ((it / STAGES) - 1) & 1)) {
             tc::record_error(tc::kErrTimeoutEmpty);
             ok = false;
             break;
           }
-          tc::mbar_arrive_expect_tx(&full_x[s], L::kXTile);
-          tc::tma_load_2d(smem + s * L::kStage, &tmap_x, kt * kBK, m0, &full_x[s]);
+          // two boxes of 64 k on one barrier (the second may lie past K: zero-filled)
+          tc::mbar_arrive_expect_tx(&full_x[s], 2 * L::kXTile);
+          tc::tma_load_2d(smem + s * L::kStage, &tmap_x, G * kStageK, m0, &full_x[s]);
+          tc::tma_load_2d(smem + s * L::kStage + L::kXTile, &tmap_x, G * kStageK + kBK, m0, &full_x[s]);
         }
       }
       // never leave the CTA while a copy into its shared memory is in flight
@@ -225,9 +229,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT);
         int tile, split, g0, g1;
         tc_unit(a, blockIdx.x + j * gridDim.x, a.Kp >> 7, tile, split, g0, g1);
-        const int kt0 = 2 * g0, kt1 = min(2 * g1, KT);
-        for (int kt = kt0; kt < kt1; kt++) {
-          const int w = (kt >> 1) & 1;  // warpgroup that dequantised this stage
+#pragma unroll 2
+        for (int G = g0; G < g1; G++) {
+          const int w = G & 1;  // warpgroup that dequantised this stage
           const int as = w ? kAPer + aslot1 : aslot0;
           const uint32_t aph = w ? aph1 : aph0;
           if (w) {
@@ -243,10 +247,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc::tc_fence_after();
           const uint64_t bdesc = desc0 + (uint64_t)((uint32_t)(xslot * L::kStage) >> 4);
           const uint32_t at = tmem_base + kAColBase + (uint32_t)(as * kAStageCols);
+          // eight K = 16 slices: slice kk reads box kk / 4 at byte 32 * (kk % 4)
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; kk++)
-            tc::umma_f16_ta(tmem_d, at + (uint32_t)(kk * 8), bdesc + (uint64_t)(kk * 2), idesc,
-                            (kt > kt0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kStageK / 16; kk++)
+            tc::umma_f16_ta(tmem_d, at + (uint32_t)(kk * 8),
+                            bdesc + (uint64_t)(((kk >> 2) * L::kXTile + (kk & 3) * 32) >> 4), idesc,
+                            (G > g0 || kk > 0) ? 1u : 0u);
           tc::umma_commit(&empty_x[xslot]);
           tc::umma_commit(&empty_a[as]);
           if (++xslot == STAGES) { xslot = 0; xph ^= 1u; }
@@ -350,19 +356,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint2 gs = (LAYOUT == 1) ? *reinterpret_cast<const uint2*>(sring + slot * kSSlot + r * 8)
                                        : make_uint2(0, 0);
         const uint8_t* kscale = sring + slot * kSSlot + wl * 256;
+        const int c = acnt++;
+        const int s = wg * kAPer + c % kAPer;  // A slot in this warpgroup's sub-ring
+        // warp-uniform outcome: tcgen05.st and the per-warp arrival below are warp-collective
+        if (c >= kAPer && !__all_sync(0xffffffffu, tc::mbar_wait(&empty_a[s], ((c / kAPer) - 1) & 1))) {
+          tc::record_error(tc::kErrTimeoutEmpty);
+          ok = false;
+          break;
+        }
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-          const int kt = 2 * G + h;
-          if (kt >= KT) break;
-          const int c = acnt++;
-          const int s = wg * kAPer + c % kAPer;  // A slot in this warpgroup's sub-ring
-          // warp-uniform outcome: tcgen05.st and the per-warp arrival below are warp-collective
-          if (c >= kAPer && !__all_sync(0xffffffffu, tc::mbar_wait(&empty_a[s], ((c / kAPer) - 1) & 1))) {
-            tc::record_error(tc::kErrTimeoutEmpty);
-            ok = false;
-            break;
-          }
-          // word (t, 2h+ii) holds local k = 32*ii + 8t .. +7, i.e. TMEM columns 16*ii + 4t .. +3
+          // word (t, 2h+ii) holds local k = 64h + 32*ii + 8t .. +7, i.e. TMEM
+          // columns 32h + 16*ii + 4t .. +3 of the stage
           uint32_t av[32];
 #pragma unroll
           for (int t = 0; t < 4; t++) {
@@ -389,13 +394,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               for (int e = 0; e < 4; e++) av[16 * ii + 4 * t + e] = d[e];
             }
           }
-          tc::tmem_st_32x32b_x32(tmem_base + ((uint32_t)(32 * wl) << 16) + kAColBase + (uint32_t)(s * kAStageCols),
-                                 av);
-          tc::tmem_st_wait();
-          tc::tc_fence_before();
-          __syncwarp();  // the warp's 32 lanes have stored: one arrival for the warp
-          if (lane == 0) tc::mbar_arrive(&full_a[s]);
+          tc::tmem_st_32x32b_x32(
+              tmem_base + ((uint32_t)(32 * wl) << 16) + kAColBase + (uint32_t)(s * kAStageCols + 32 * h), av);
         }
+        tc::tmem_st_wait();
+        tc::tc_fence_before();
+        __syncwarp();  // the warp's 32 lanes have stored: one arrival for the warp
+        if (lane == 0) tc::mbar_arrive(&full_a[s]);
       }
     }
     cp_async_wait<0>();  // no copy into shared memory may outlive the loop
@@ -628,11 +633,11 @@ static size_t tc_ws_bytes(int N, int M, int bt, int splits) {
 // two 128-k groups, when the workspace holds the plan's ws_bytes.
 static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
   struct Cand { int bt, nacc; };
-  const Cand cands[] = {{64, 2}, {128, 2}, {192, 2}, {224, 1}, {256, 1}};
+  const Cand cands[] = {{64, 2}, {128, 2}, {192, 1}, {224, 1}, {256, 1}};
   const int splits_c[] = {1, 2, 3, 4, 6, 8};  // the reduction unrolls up to 8 slices
   const long long n_tiles = (N + 127) / 128;
   const int KG = padded_k(K) / 128;
-  const long long KT = (K + kBK - 1) / kBK;
+  const long long KT = KG;  // 128-k stages per tile
   TcPlan best;
   long long best_cost = -1;
   for (const Cand& c : cands) {
@@ -645,7 +650,7 @@ static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
       const long long units = tiles * S;
       const long long rounds = (units + sms - 1) / sms;
       const long long stages = (KT + S - 1) / S;
-      long long cost = rounds * stages * (450 + 2 * c.bt);
+      long long cost = rounds * stages * (640 + 4 * c.bt);
       if (c.nacc == 1) cost += (rounds - 1) * 8 * c.bt;
       if (S > 1) cost += rounds * (10000 + 16LL * S * c.bt);
       if (best_cost < 0 || cost < best_cost) {
@@ -687,19 +692,19 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   }
   if (layout == 1) {
     switch (p.bt) {
-      case 64: return launch_tc_t<1, 64, 8, 2>(a, x, ldx, st, pdl);
-      case 128: return launch_tc_t<1, 128, 8, 2>(a, x, ldx, st, pdl);
-      case 192: return launch_tc_t<1, 192, 4, 2>(a, x, ldx, st, pdl);
-      case 224: return launch_tc_t<1, 224, 4, 1>(a, x, ldx, st, pdl);
-      default: return launch_tc_t<1, 256, 4, 1>(a, x, ldx, st, pdl);
+      case 64: return launch_tc_t<1, 64, 4, 2>(a, x, ldx, st, pdl);
+      case 128: return launch_tc_t<1, 128, 3, 2>(a, x, ldx, st, pdl);
+      case 192: return launch_tc_t<1, 192, 3, 1>(a, x, ldx, st, pdl);
+      case 224: return launch_tc_t<1, 224, 2, 1>(a, x, ldx, st, pdl);
+      default: return launch_tc_t<1, 256, 2, 1>(a, x, ldx, st, pdl);
     }
   }
   switch (p.bt) {
-    case 64: return launch_tc_t<0, 64, 8, 2>(a, x, ldx, st, pdl);
-    case 128: return launch_tc_t<0, 128, 8, 2>(a, x, ldx, st, pdl);
-    case 192: return launch_tc_t<0, 192, 4, 2>(a, x, ldx, st, pdl);
-    case 224: return launch_tc_t<0, 224, 4, 1>(a, x, ldx, st, pdl);
-    default: return launch_tc_t<0, 256, 4, 1>(a, x, ldx, st, pdl);
+    case 64: return launch_tc_t<0, 64, 4, 2>(a, x, ldx, st, pdl);
+    case 128: return launch_tc_t<0, 128, 3, 2>(a, x, ldx, st, pdl);
+    case 192: return launch_tc_t<0, 192, 3, 1>(a, x, ldx, st, pdl);
+    case 224: return launch_tc_t<0, 224, 2, 1>(a, x, ldx, st, pdl);
+    default: return launch_tc_t<0, 256, 2, 1>(a, x, ldx, st, pdl);
   }
 }
 
