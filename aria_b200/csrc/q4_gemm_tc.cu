@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp < 8) {
     // ------------------------------------------------------------ dequantisers
     // Two warpgroups: WG w (warps 4w..4w+3) owns the 128-k groups G = w, w+2, ...
-    // of every tile and feeds both of their 64-k stages.  Each thread owns one
+    // of every tile and feeds their 128-k stages.  Each thread owns one
     // weight row (= TMEM lane); each warp streams its 32 rows' 64-byte code
     // groups plus their scales into a kQDepth-deep shared-memory ring with
     // 16-byte cp.async, so loads run groups ahead without holding registers; the
@@ -623,14 +623,15 @@ static size_t tc_ws_bytes(int N, int M, int bt, int splits) {
 }
 
 // Token-tile height BT and K split by a cost model: rounds of CTAs (work units
-// / SMs, rounded up) x 64-k stages per unit x (fixed issue cost of a stage + 2
+// / SMs, rounded up) x 128-k stages per unit x (fixed issue cost of a stage + 4
 // cycles per token), plus, for a single accumulator, the exposed epilogue of
 // every round after the first, plus, for a K split, each unit's partial write
 // and the last unit's reduction (measured: 7-9 us per round at 64 tokens, fit
-// as 10000 + 16 * S * BT in the same units).  The fixed ~450 cycles per stage is the MMA
-// issuer's latency (two barrier waits, a fence, four MMAs and two commits).  K
-// splits are considered for 64- and 128-token tiles, with every slice at least
-// two 128-k groups, when the workspace holds the plan's ws_bytes.
+// as 10000 + 16 * S * BT in the same units).  The fixed ~640 cycles per stage
+// is the MMA issuer's latency (two barrier waits, a fence, eight MMAs and two
+// commits).  K splits are considered for 64- and 128-token tiles, with every
+// slice at least two 128-k groups, when the workspace holds the plan's
+// ws_bytes.
 static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
   struct Cand { int bt, nacc; };
   const Cand cands[] = {{64, 2}, {128, 2}, {192, 1}, {224, 1}, {256, 1}};
