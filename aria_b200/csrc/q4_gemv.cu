@@ -484,17 +484,101 @@ struct GemvPlan {
   size_t smem = 0;
 };
 
+// One-time (per device) attributes of a kernel instance: all of shared memory
+// may be requested, and the carveout keeps the SM in one configuration across a
+// chain of projections, so the next kernel's CTA can become resident beside this one.
+template <int LAYOUT, int R, int P>
+static cudaError_t gemv_configure() {
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (configured_dev == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kGemvSmemMax);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  configured_dev = dev;
+  return cudaSuccess;
+}
+
+// Clusters of C CTAs that can be resident at once with per_sm CTAs' worth of
+// shared memory each.  A cluster must fit inside one GPC, so on a part whose
+// GPCs hold unequal SM counts fewer than sms * per_sm / C fit (B200: 33 clusters
+// of 4 at one CTA per SM, 71 at two, but all 74 / 148 clusters of 2); a plan
+// beyond this count would run a second wave.  Cached per device.
+template <int LAYOUT, int R, int P>
+static int gemv_max_clusters_t(int C, int per_sm, int fallback) {
+  if (gemv_configure<LAYOUT, R, P>() != cudaSuccess) {
+    cudaGetLastError();
+    return fallback;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C * 64);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = per_sm == 2 ? kGemvSmemHalf : kGemvSmemMax;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemv_stream_kernel<LAYOUT, R, P>, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return fallback;
+  }
+  return n;
+}
+
+static int gemv_max_clusters(int layout, int R, int P, int C, int per_sm, int sms) {
+  const int fallback = std::max(1, sms * per_sm / C);
+  if (C == 1) return fallback;
+  constexpr int kDevices = 64;
+  static int cache[kDevices][2][2][2][2][2];  // [dev][layout][R-1][P-1][C==4][per_sm-1]; 0 = not queried
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevices) {
+    cudaGetLastError();
+    return fallback;
+  }
+  int& slot = cache[dev][layout & 1][R - 1][P - 1][C == 4 ? 1 : 0][per_sm - 1];
+  if (slot == 0) {
+    // not a stream operation; relaxed capture mode keeps a first call made while
+    // the thread captures a CUDA graph from invalidating that capture
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    int n;
+    if (layout == 1)
+      n = R == 2 ? (P == 2 ? gemv_max_clusters_t<1, 2, 2>(C, per_sm, fallback) : gemv_max_clusters_t<1, 2, 1>(C, per_sm, fallback))
+                 : (P == 2 ? gemv_max_clusters_t<1, 1, 2>(C, per_sm, fallback) : gemv_max_clusters_t<1, 1, 1>(C, per_sm, fallback));
+    else
+      n = R == 2 ? (P == 2 ? gemv_max_clusters_t<0, 2, 2>(C, per_sm, fallback) : gemv_max_clusters_t<0, 2, 1>(C, per_sm, fallback))
+                 : (P == 2 ? gemv_max_clusters_t<0, 1, 2>(C, per_sm, fallback) : gemv_max_clusters_t<0, 1, 1>(C, per_sm, fallback));
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    slot = std::min(n, fallback);
+  }
+  return slot;
+}
+
 // Picks the tile height (16 or 32 rows), the groups per chunk (1 or 2), the
 // cluster K split (1, 2 or 4) and two or one CTAs per SM (two when their
-// shared memory allows: 16 warps per SM, and a CTA of the next kernel in a
-// chain can become resident as soon as one of this kernel's CTAs exits).
-// Cost model, in issue slots of the longest warp: each chunk costs a fixed
-// ~120 (copies, waits, reductions shared out) plus ~100 per 16-row x 128-k
-// block, x1.25 when two CTAs share an SM's issue slots (measured: two 8-warp
-// CTAs per SM hide latency better than one, so they are not twice as slow); a
-// cluster split adds ~6000 (two cluster barriers and the distributed-shared-
-// memory reduction).
-static bool plan_gemv(int K, int N, int M, int sms, GemvPlan& best) {
+// shared memory allows).  Cost model, fitted to timings of every feasible plan
+// of the Efkolos and d_model-4096 projections at M = 1 and 8 on B200 (chains of
+// launches, weights larger than L2; the chosen plan is within 2% of the fastest
+// on average, 8.5% at worst), in units of ~3.5 ns:
+//   chunks of the longest warp x (100 + 150 per 16-row x 128-k block)
+//     (x1.4 when two CTAs share an SM)
+//   + 300 per row tile of a CTA (partial-sum reduction and store)
+//   + 20 per token row and 128-k group of activations staged per SM (the
+//     prologue copies them from L2 before the weight stream starts)
+//   + 3000 for a cluster split (cluster barriers, distributed-shared-memory sums).
+// The kernel is bound by how fast its few chunks per warp arrive rather than by
+// arithmetic (dropping all arithmetic leaves the time unchanged), hence the large
+// per-chunk term.
+static bool plan_gemv(int layout, int K, int N, int M, int sms, GemvPlan& best) {
   const int KG = padded_k(K) / 128;
   long long best_cost = -1;
   for (int C : {1, 2, 4}) {
@@ -508,14 +592,16 @@ static bool plan_gemv(int K, int N, int M, int sms, GemvPlan& best) {
         if (P == 2 && gw < 2) continue;
         const int tiles = (N + 16 * R - 1) / (16 * R);
         for (int per_sm : {2, 1}) {
-          const int clusters = std::min(tiles, std::max(1, sms * per_sm / C));
+          const int clusters = std::min(tiles, gemv_max_clusters(layout, R, P, C, per_sm, sms));
           const int tpc = (tiles + clusters - 1) / clusters;
           if (C > 1 && tpc > kGemvMaxTilesCta) continue;
           const long long chunks = (long long)tpc * ((gw + P - 1) / P);  // per warp
           const size_t smem = R == 2 ? (P == 2 ? gemv_smem<2, 2>(C, xbytes, chunks) : gemv_smem<2, 1>(C, xbytes, chunks))
                                      : (P == 2 ? gemv_smem<1, 2>(C, xbytes, chunks) : gemv_smem<1, 1>(C, xbytes, chunks));
           if (smem > (per_sm == 2 ? kGemvSmemHalf : kGemvSmemMax)) continue;
-          const long long cost = chunks * (120 + 100 * R * P) * (per_sm == 2 ? 5 : 4) / 4 + (C > 1 ? 6000 : 0);
+          const int ctas_per_sm = std::min(per_sm, (clusters * C + sms - 1) / sms);
+          const long long cost = chunks * (100 + 150 * R * P) * (per_sm == 2 ? 7 : 5) / 5 + 300LL * tpc +
+                                 20LL * ctas_per_sm * M * gmax + (C > 1 ? 3000 : 0);
           if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             best.R = R;
@@ -537,21 +623,8 @@ static bool plan_gemv(int K, int N, int M, int sms, GemvPlan& best) {
 
 template <int LAYOUT, int R, int P>
 static cudaError_t launch_gemv_t(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
-  static int configured_dev = -1;  // the attributes are per device; set once per device in use
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  cudaError_t e = gemv_configure<LAYOUT, R, P>();
   if (e != cudaSuccess) return e;
-  if (configured_dev != dev) {
-    e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kGemvSmemMax);
-    if (e != cudaSuccess) return e;
-    // all shared memory: the SM keeps one configuration across a chain of
-    // projections, so the next kernel's CTA can become resident beside this one
-    e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             (int)cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
-    configured_dev = dev;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.clusters * a.C);
   cfg.blockDim = dim3(kGemvThreads);
@@ -588,14 +661,14 @@ static cudaError_t launch_gemv_layout(const GemvArgs& a, const GemvPlan& p, cuda
 bool gemv_supported(int K, int N, int M) {
   if (M < 1 || M > kGemvMaxM) return false;
   GemvPlan p;
-  return plan_gemv(K, N, M, device_sms(), p);
+  return plan_gemv(0, K, N, M, device_sms(), p) && plan_gemv(1, K, N, M, device_sms(), p);
 }
 
 cudaError_t launch_gemv(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                         int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
                         bool const_weights) {
   GemvPlan p;
-  if (!plan_gemv(K, N, M, device_sms(), p)) return cudaErrorInvalidValue;
+  if (!plan_gemv(layout, K, N, M, device_sms(), p)) return cudaErrorInvalidValue;
   GemvArgs a;
   a.qs = tiled;
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
