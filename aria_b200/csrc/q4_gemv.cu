@@ -166,9 +166,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
   const int C = a.C;
   const int crank = (int)blockIdx.x % C;
   const int q = (int)blockIdx.x / C;
-  const int t0 = (int)((long long)q * a.tiles / a.clusters);
-  const int t1 = (int)((long long)(q + 1) * a.tiles / a.clusters);
-  const int ntl = t1 - t0;
+  // row tiles q, q + clusters, q + 2 clusters, ...: at any moment the clusters
+  // stream neighbouring tiles, so the weight reads advance through memory as one front
+  const int tstep = a.clusters;
+  const int ntl = q < a.tiles ? (a.tiles - 1 - q) / tstep + 1 : 0;
   const int gc0 = crank * a.KG / C, gc1 = (crank + 1) * a.KG / C;
   const int gw0 = gc0 + warp * (gc1 - gc0) / kGemvWarps;
   const int gw1 = gc0 + (warp + 1) * (gc1 - gc0) / kGemvWarps;
@@ -201,12 +202,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
     sc_off[v] = LAYOUT == 1 ? ((size_t)sc_h[v] * a.N + sc_row[v]) * 4 : (size_t)lane * 8;
   }
   const bool sc_lane = LAYOUT == 1 ? lane < P * TR : lane < 16 * P;  // lane has a first scale piece
-  int is_j = t0, is_s = 0, is_slot = 0, is_G = gw0;
+  int is_j = q, is_s = 0, is_slot = 0, is_G = gw0;
   const uint8_t* is_src = lane_qs + (size_t)is_j * TR * RB + (size_t)gw0 * 64;
   const __half* is_ssrc = LAYOUT == 1 ? a.scales + ((size_t)gw0 * a.N + (size_t)is_j * TR) * 4
                                       : a.scales + (size_t)((is_j * TR) >> 5) * a.Kp + (size_t)gw0 * 128;
   auto issue_next = [&]() {
-    if (is_j < t1 && ns > 0) {
+    if (is_j < a.tiles && ns > 0) {
       const int r0 = is_j * TR;
       const uint32_t st = my_ring + (uint32_t)is_slot * S::kStage + lane_dst;
       const uint32_t sst = my_ring + (uint32_t)is_slot * S::kStage + S::kCodeBytes;
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
       // advance to the next chunk of the warp's sequence
       if (++is_s == ns) {
         is_s = 0;
-        ++is_j;
+        is_j += tstep;
         is_G = gw0;
         is_src = lane_qs + (size_t)is_j * TR * RB + (size_t)gw0 * 64;
         is_ssrc = LAYOUT == 1 ? a.scales + ((size_t)gw0 * a.N + (size_t)is_j * TR) * 4
@@ -270,7 +271,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
     for (int i = 0; i < D; i++) issue_next();
   } else if (ns > 0 && ntl > 0 && lane < TR) {
     // warm L2 with this warp's slice of the first tile (rows may be written by the previous kernel)
-    const int n = t0 * TR + lane;
+    const int n = q * TR + lane;
     if (n < a.N) bulk_prefetch_l2(a.qs + (size_t)n * RB + (size_t)gw0 * 64, (uint32_t)(gw1 - gw0) * 64u);
   }
   grid_dep_launch();
@@ -296,7 +297,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
   // bias of the first tile this warp stores (tile number warp), loaded while the copies fly
   const int pre_tile = warp;
   float bias_pre[R][2];
-  gemv_load_bias<R>(a, bias_pre, (t0 + pre_tile) * TR, g);
+  gemv_load_bias<R>(a, bias_pre, (q + pre_tile * tstep) * TR, g);
   cp_async_wait<0>();
   __syncthreads();
 
@@ -409,9 +410,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
 #pragma unroll
           for (int r = 0; r < R; r++) { bia[r][0] = bias_pre[r][0]; bia[r][1] = bias_pre[r][1]; }
         } else {
-          gemv_load_bias<R>(a, bia, (t0 + jl) * TR, g);
+          gemv_load_bias<R>(a, bia, (q + jl * tstep) * TR, g);
         }
-        gemv_store_tile<R>(a, tot, bia, (t0 + jl) * TR, g, t);
+        gemv_store_tile<R>(a, tot, bia, (q + jl * tstep) * TR, g, t);
       }
     }
   }
@@ -448,9 +449,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
 #pragma unroll
           for (int r = 0; r < R; r++) { bia[r][0] = bias_pre[r][0]; bia[r][1] = bias_pre[r][1]; }
         } else {
-          gemv_load_bias<R>(a, bia, (t0 + jl) * TR, g);
+          gemv_load_bias<R>(a, bia, (q + jl * tstep) * TR, g);
         }
-        gemv_store_tile<R>(a, tot, bia, (t0 + jl) * TR, g, t);
+        gemv_store_tile<R>(a, tot, bia, (q + jl * tstep) * TR, g, t);
       }
     }
     cluster_sync_all();  // peers keep their shared memory until rank 0 has read it
