@@ -134,6 +134,36 @@ __device__ __forceinline__ void dequant_word_f16x2(uint32_t w, uint32_t out[4]) 
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out[3]) : "r"(hi1), "r"(k1_16), "r"(km72));
 }
 
+// dequant_word_f16x2 of two words wa (A-fragment row g) and wb (row g + 8),
+// written straight into the register order of the two m16n8k16 A fragments
+// that consume them: A1 = k pairs (e0,e1) and (e2,e3), A2 = (e4,e5) and
+// (e6,e7), each as {row g, row g + 8} for the low and then the high k half.
+// Same 18 instructions as two dequant_word_f16x2 calls; the operands need no
+// reordering before the MMAs.
+__device__ __forceinline__ void dequant_pair_mma(uint32_t wa, uint32_t wb, uint32_t A1[4], uint32_t A2[4]) {
+  const uint32_t k1032 = 0x64086408u;  // f16x2 (1032, 1032)
+  const uint32_t k1_16 = 0x2C002C00u;  // f16x2 (1/16, 1/16)
+  const uint32_t km72 = 0xD480D480u;   // f16x2 (-72, -72)
+  const uint32_t wa2 = wa >> 8, wb2 = wb >> 8;
+  uint32_t t0, t1, t2, t3, t4, t5, t6, t7;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(t0) : "r"(wa));
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(t1) : "r"(wb));
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64006400, 0xEA;" : "=r"(t2) : "r"(wa));
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64006400, 0xEA;" : "=r"(t3) : "r"(wb));
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(t4) : "r"(wa2));
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(t5) : "r"(wb2));
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64006400, 0xEA;" : "=r"(t6) : "r"(wa2));
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64006400, 0xEA;" : "=r"(t7) : "r"(wb2));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(A1[0]) : "r"(t0), "r"(k1032));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(A1[1]) : "r"(t1), "r"(k1032));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(A1[2]) : "r"(t2), "r"(k1_16), "r"(km72));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(A1[3]) : "r"(t3), "r"(k1_16), "r"(km72));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(A2[0]) : "r"(t4), "r"(k1032));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(A2[1]) : "r"(t5), "r"(k1032));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(A2[2]) : "r"(t6), "r"(k1_16), "r"(km72));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(A2[3]) : "r"(t7), "r"(k1_16), "r"(km72));
+}
+
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));

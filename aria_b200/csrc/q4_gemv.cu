@@ -149,7 +149,9 @@ __device__ __forceinline__ void gemv_load_bias(const GemvArgs& a, float (&b)[R][
     }
 }
 
-template <int LAYOUT, int R, int P>
+// ONE: a single token row (M = 1), NK only: the block-scale FMAs of the unused
+// odd token columns are left out.
+template <int LAYOUT, int R, int P, bool ONE = false>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const GemvArgs a) {
   using S = GemvShape<R, P>;
   constexpr int D = S::kDepth;
@@ -356,20 +358,22 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
           for (int r = 0; r < R; r++) {
             const uint32_t wa = i4 == 0 ? qa[r].x : (i4 == 1 ? qa[r].y : (i4 == 2 ? qa[r].z : qa[r].w));
             const uint32_t wb = i4 == 0 ? qb[r].x : (i4 == 1 ? qb[r].y : (i4 == 2 ? qb[r].z : qb[r].w));
-            uint32_t pa[4], pb[4];
-            dequant_word_f16x2(wa, pa);
-            dequant_word_f16x2(wb, pb);
+            uint32_t A1[4], A2[4];
+            dequant_pair_mma(wa, wb, A1, A2);
             if (LAYOUT == 1) {
               float c[4];
-              mma_16816_z(c, pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
-              mma_16816(c, pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+              mma_16816_z(c, A1[0], A1[1], A1[2], A1[3], xv.x, xv.y);
+              mma_16816(c, A2[0], A2[1], A2[2], A2[3], xv.z, xv.w);
+              // c[1], c[3] are token column 2t + 1 >= 1: not needed for one token
               acc[r][0] = fmaf(sa[r][i4], c[0], acc[r][0]);
-              acc[r][1] = fmaf(sa[r][i4], c[1], acc[r][1]);
               acc[r][2] = fmaf(sb[r][i4], c[2], acc[r][2]);
-              acc[r][3] = fmaf(sb[r][i4], c[3], acc[r][3]);
+              if (!ONE) {
+                acc[r][1] = fmaf(sa[r][i4], c[1], acc[r][1]);
+                acc[r][3] = fmaf(sb[r][i4], c[3], acc[r][3]);
+              }
             } else {
-              mma_16816(acc[r], pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
-              mma_16816(acc[r], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+              mma_16816(acc[r], A1[0], A1[1], A1[2], A1[3], xv.x, xv.y);
+              mma_16816(acc[r], A2[0], A2[1], A2[2], A2[3], xv.z, xv.w);
             }
           }
         }
@@ -488,17 +492,17 @@ struct GemvPlan {
 // One-time (per device) attributes of a kernel instance: all of shared memory
 // may be requested, and the carveout keeps the SM in one configuration across a
 // chain of projections, so the next kernel's CTA can become resident beside this one.
-template <int LAYOUT, int R, int P>
+template <int LAYOUT, int R, int P, bool ONE = false>
 static cudaError_t gemv_configure() {
   static int configured_dev = -1;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (configured_dev == dev) return cudaSuccess;
-  e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P, ONE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kGemvSmemMax);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P>, cudaFuncAttributePreferredSharedMemoryCarveout,
+  e = cudaFuncSetAttribute(gemv_stream_kernel<LAYOUT, R, P, ONE>, cudaFuncAttributePreferredSharedMemoryCarveout,
                            (int)cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
   configured_dev = dev;
@@ -622,9 +626,9 @@ static bool plan_gemv(int layout, int K, int N, int M, int sms, GemvPlan& best) 
   return best_cost >= 0;
 }
 
-template <int LAYOUT, int R, int P>
+template <int LAYOUT, int R, int P, bool ONE>
 static cudaError_t launch_gemv_t(const GemvArgs& a, size_t smem, cudaStream_t st, bool pdl) {
-  cudaError_t e = gemv_configure<LAYOUT, R, P>();
+  cudaError_t e = gemv_configure<LAYOUT, R, P, ONE>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.clusters * a.C);
@@ -647,14 +651,22 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, size_t smem, cudaStream_t st
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<LAYOUT, R, P>, a);
+  return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<LAYOUT, R, P, ONE>, a);
 }
 
 template <int LAYOUT>
 static cudaError_t launch_gemv_layout(const GemvArgs& a, const GemvPlan& p, cudaStream_t st, bool pdl) {
-  if (p.R == 2) return p.P == 2 ? launch_gemv_t<LAYOUT, 2, 2>(a, p.smem, st, pdl)
-                                : launch_gemv_t<LAYOUT, 2, 1>(a, p.smem, st, pdl);
-  return p.P == 2 ? launch_gemv_t<LAYOUT, 1, 2>(a, p.smem, st, pdl) : launch_gemv_t<LAYOUT, 1, 1>(a, p.smem, st, pdl);
+  constexpr bool kNK = LAYOUT == 1;
+  if (kNK && a.M == 1) {
+    if (p.R == 2) return p.P == 2 ? launch_gemv_t<LAYOUT, 2, 2, kNK>(a, p.smem, st, pdl)
+                                  : launch_gemv_t<LAYOUT, 2, 1, kNK>(a, p.smem, st, pdl);
+    return p.P == 2 ? launch_gemv_t<LAYOUT, 1, 2, kNK>(a, p.smem, st, pdl)
+                    : launch_gemv_t<LAYOUT, 1, 1, kNK>(a, p.smem, st, pdl);
+  }
+  if (p.R == 2) return p.P == 2 ? launch_gemv_t<LAYOUT, 2, 2, false>(a, p.smem, st, pdl)
+                                : launch_gemv_t<LAYOUT, 2, 1, false>(a, p.smem, st, pdl);
+  return p.P == 2 ? launch_gemv_t<LAYOUT, 1, 2, false>(a, p.smem, st, pdl)
+                  : launch_gemv_t<LAYOUT, 1, 1, false>(a, p.smem, st, pdl);
 }
 
 // true when the streaming kernel takes this shape (M <= 8 and the CTA's
