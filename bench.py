@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLAS fp16 same-box reference point")
     ap.add_argument("--prefill", type=lambda v: [int(t) for t in v.split(",") if t], default=[4096, 8192])
     ap.add_argument("--batched", type=lambda v: [int(t) for t in v.split(",") if t], default=[16, 64, 256])
     ap.add_argument("--scaled", type=int, default=1, help="1: also run BASELINE configs[4] (d_model 4096)")
@@ -260,6 +261,87 @@ def gemv_config4_b1(stream, timed, l2: int, hbm_peak: float) -> dict:
     return out
 
 
+def cublas_fp16_section(stream, timed, l2: int, q4_decode_ms: float, q4_prefill_ms: dict) -> dict:
+    """The reference's own GPU op on the same box and shapes, as a reference
+    point: cuBLAS fp16 GEMM on f16 weights (the reference's gemm(),
+    lold3344/ARIA src/transformer_cuda.rs:615-640, reached here through
+    torch.matmul), with no Q4_0 kernel involved.  Efkolos decode step at M = 1
+    (the 81 projections chained in a CUDA graph, weight replicas > 4x L2
+    rotated), the config-4 LM head at M = 1 (copies > 4x L2), and the Efkolos
+    prefill step at M = 4096."""
+    import torch
+    from aria_b200.efkolos import EFKOLOS, SCALED
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+
+    def f16(shape, sigma):
+        return torch.randn(shape, generator=gen, device="cuda", dtype=torch.float16) * sigma
+
+    projs = EFKOLOS.all_projections()
+    f16_bytes = sum(K * N * 2 for (_, _, K, N, _) in projs)
+    reps = max(2, -(-4 * l2 // f16_bytes))
+    # weights as the reference holds them: KN w[k][n] (x @ w), NK embed[n][k] (x @ embed^T)
+    replicas = [[f16((K, N) if lay == 0 else (N, K), sg) for (_, lay, K, N, sg) in projs] for _ in range(reps)]
+    out = {"op": "torch.matmul -> cuBLAS fp16 GEMM, f16 weights (the reference's gemm())"}
+
+    def chain(ws, M):
+        xs = [f16((M, K), 1.0) for (_, _, K, _, _) in projs]
+        ys = [torch.empty(M, N, device="cuda", dtype=torch.float16) for (_, _, _, N, _) in projs]
+        def run():
+            for (_, lay, K, N, _), w, x, y in zip(projs, ws, xs, ys):
+                torch.matmul(x, w if lay == 0 else w.t(), out=y)
+        return run
+
+    graphs = []
+    with torch.cuda.stream(stream):
+        for ws in replicas:
+            run = chain(ws, 1)
+            run()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run()
+            graphs.append(g)
+    ms = timed(lambda i: graphs[i % reps].replay(), 50, 5, "cublas_decode_step") / 50
+    out["decode_b1"] = {"ms_per_step": ms, "weight_bytes_f16": f16_bytes,
+                        "GBs": (f16_bytes + 2 * sum(K + N for (_, _, K, N, _) in projs)) / (ms * 1e-3) / 1e9,
+                        "q4_step_speedup": ms / q4_decode_ms}
+    del graphs
+    # config-4 LM head at one token
+    (_, _, K, N, sg) = SCALED.lm_head()
+    ncopy = max(2, -(-4 * l2 // (K * N * 2)))
+    embeds = [f16((N, K), sg) for _ in range(ncopy)]
+    x = f16((1, K), 1.0)
+    y = torch.empty(1, N, device="cuda", dtype=torch.float16)
+    n = 16
+    with torch.cuda.stream(stream):
+        torch.matmul(x, embeds[0].t(), out=y)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for j in range(n):
+                torch.matmul(x, embeds[j % ncopy].t(), out=y)
+    us = timed(lambda i: g.replay(), 10, 3, "cublas_lm_head_config4") * 1e3 / (10 * n)
+    out["lm_head_config4_b1"] = {"us_per_launch": us, "GBs": (K * N * 2 + 2 * (K + N)) / (us * 1e-6) / 1e9}
+    del g, embeds
+    # prefill step
+    for M, q4_ms in q4_prefill_ms.items():
+        with torch.cuda.stream(stream):
+            run = chain(replicas[0], M)
+            run()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run()
+        pms = timed(lambda i: g.replay(), 5, 2, f"cublas_prefill_M{M}") / 5
+        out[f"prefill_M{M}"] = {"ms_per_step": pms, "TFLOPs": M * EFKOLOS.flops_per_token() / (pms * 1e-3) / 1e12,
+                                "q4_step_speedup": pms / q4_ms}
+        del g
+    del replicas
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
@@ -430,6 +512,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                             "frac_of_measured_sustained_peak": tf / world / bf16_sus}
         del g, pprog
         torch.cuda.empty_cache()
+    cublas = None
+    if rank == 0 and world == 1 and not args.no_cublas:
+        cublas = cublas_fp16_section(stream, timed, l2, ms_step,
+                                     {4096: prefill["M4096"]["ms_per_step"]} if "M4096" in prefill else {})
     scaled = None
     if args.scaled:
         scaled = scaled_section(args, rank, world, local_rank, stream, timed, peaks)
@@ -456,6 +542,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                        "peak_tflops_sustained": bf16_sus, **prefill},
            "scaled": scaled,
            "gemv_config4_b1": gemv_large,
+           "cublas_fp16_same_box": cublas,
            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": prog.input_bytes(),
                    "d2h_bytes_per_step": prog.ys[-1].numel() * 2, "ms_per_step": e2e_ms},
            "gpu_launches": prog.launches * args.steps}
