@@ -20,6 +20,7 @@ FLAG_CONST_WEIGHTS = 1
 FLAG_KERNEL_STREAM = 2
 FLAG_KERNEL_REGISTER = 4
 FLAG_KERNEL_TENSOR = 8
+FLAG_EPILOGUE_GELU = 16
 F32, F16 = 0, 1
 
 # every symbol include/aria_q4.h declares: (restype, argtypes)

@@ -169,7 +169,7 @@ int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint1
   if (y_dtype != ARIA_Q4_F16 && y_dtype != ARIA_Q4_F32) return ARIA_Q4_EINVAL;
   if (ldx < K || ldy < N) return ARIA_Q4_EINVAL;
   const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_STREAM | ARIA_Q4_FLAG_KERNEL_REGISTER |
-                    ARIA_Q4_FLAG_KERNEL_TENSOR;
+                    ARIA_Q4_FLAG_KERNEL_TENSOR | ARIA_Q4_FLAG_EPILOGUE_GELU;
   if ((flags & ~known) != 0) return ARIA_Q4_EINVAL;
   if (((uintptr_t)tiled & 255u) != 0 || !aligned16(x) || (ldx % 8) != 0) return ARIA_Q4_EALIGN;
   if (workspace_bytes == 0) workspace = nullptr;
@@ -179,13 +179,15 @@ int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint1
   const int kern = choose_kernel(K, N, M, workspace != nullptr, flags);
   if (kern < 0) return -kern;
   const bool cw = (flags & ARIA_Q4_FLAG_CONST_WEIGHTS) != 0;
+  // the kernels' output code: dtype in bit 0, GELU epilogue in bit 1 (aria_q4::kOutGelu)
+  const int out = y_dtype | ((flags & ARIA_Q4_FLAG_EPILOGUE_GELU) ? aria_q4::kOutGelu : 0);
   if (kern == ARIA_Q4_KERNEL_STREAM)
-    return cuda_status(launch_gemv((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
+    return cuda_status(launch_gemv((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, out, ldy,
                                    (const __half*)bias, alpha, beta, st, true, cw));
   if (kern == ARIA_Q4_KERNEL_REGISTER)
-    return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
+    return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, out, ldy,
                                      (const __half*)bias, alpha, beta, st, true, cw));
-  return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
+  return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, out, ldy,
                                     (const __half*)bias, alpha, beta, workspace, workspace_bytes, st, true));
 }
 
@@ -193,7 +195,7 @@ int aria_q4_0_kernel_choice(int layout, int K, int N, int M, size_t workspace_by
   if (int s = check_tiled_shape(layout, K, N)) return -s;
   if (M < 1) return -ARIA_Q4_EINVAL;
   const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_STREAM | ARIA_Q4_FLAG_KERNEL_REGISTER |
-                    ARIA_Q4_FLAG_KERNEL_TENSOR;
+                    ARIA_Q4_FLAG_KERNEL_TENSOR | ARIA_Q4_FLAG_EPILOGUE_GELU;
   if ((flags & ~known) != 0) return -ARIA_Q4_EINVAL;
   return choose_kernel(K, N, M, workspace_bytes != 0, flags);
 }

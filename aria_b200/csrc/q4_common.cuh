@@ -228,8 +228,22 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Output code of the kernels' epilogues (internal, not ABI): bit 0 = f16 output
+// (else f32), bit 1 = GELU applied to alpha * acc + bias before the beta term.
+constexpr int kOutF16 = 1;
+constexpr int kOutGelu = 2;
+
+// GELU, tanh form, in f32 as the reference's gelu_fwd computes it
+// (lold3344/ARIA src/kernels.cu:574-583): 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
+// (Hendrycks & Gimpel's approximation; tanhf is CUDA's).
+__device__ __forceinline__ float gelu_tanh(float v) {
+  const float c = 0.7978845608f;  // sqrt(2 / pi)
+  return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
+}
+
 __device__ __forceinline__ void store_out(void* y, int ydt, size_t idx, float v, float beta) {
-  if (ydt == 0) {
+  if (ydt & kOutGelu) v = gelu_tanh(v);
+  if ((ydt & kOutF16) == 0) {
     float* yp = reinterpret_cast<float*>(y) + idx;
     if (beta != 0.0f) v += beta * *yp;
     *yp = v;

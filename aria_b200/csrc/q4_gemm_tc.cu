@@ -410,11 +410,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int rr = q * 32 + lane;
     const int KG = a.Kp >> 7;
-    // one output value: alpha * acc + bias (+ beta * y), f16 or f32
+    // one output value: [gelu](alpha * acc + bias) (+ beta * y), f16 or f32
     auto store = [&](int tok, int n, float acc, float bias) {
       float o = fmaf(a.alpha, acc, bias);
+      if (a.ydt & kOutGelu) o = gelu_tanh(o);
       const size_t idx = (size_t)tok * a.ldy + n;
-      if (a.ydt == 0) {
+      if ((a.ydt & kOutF16) == 0) {
         float* yp = reinterpret_cast<float*>(a.y) + idx;
         if (a.beta != 0.0f) o += a.beta * *yp;
         *yp = o;
@@ -450,7 +451,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int tok0 = m0 + cc * 32;
           if (!row_ok || tok0 >= a.M) continue;
           const int ntok = min(32, a.M - tok0);
-          if (a.ydt == 1 && a.beta == 0.0f) {  // f16 out, no accumulate: the common path
+          if (a.ydt == kOutF16 && a.beta == 0.0f) {  // f16 out, no activation or accumulate: the common path
             __half* yp = reinterpret_cast<__half*>(a.y) + (size_t)tok0 * a.ldy + n;
             if (ntok == 32) {
 #pragma unroll

@@ -130,6 +130,7 @@ class Q4Weight:
 
 _KERNEL_FLAGS = {"auto": 0, "stream": _lib.FLAG_KERNEL_STREAM, "register": _lib.FLAG_KERNEL_REGISTER,
                  "tensor": _lib.FLAG_KERNEL_TENSOR}
+_ACT_FLAGS = {None: 0, "gelu": _lib.FLAG_EPILOGUE_GELU}
 
 
 _WORKSPACES: dict = {}
@@ -153,8 +154,12 @@ def workspace_for(K: int, N: int, M: int, device: torch.device) -> torch.Tensor 
 
 def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bias: torch.Tensor | None = None,
            alpha: float = 1.0, beta: float = 0.0, out_dtype: torch.dtype = torch.float16,
-           const_weights: bool = False, kernel: str = "auto", workspace="auto") -> torch.Tensor:
-    """y[M, N] = alpha * x[M, K] @ W + beta * out + bias, through aria_q4_0_matmul_ex.
+           const_weights: bool = False, kernel: str = "auto", workspace="auto",
+           activation: str | None = None) -> torch.Tensor:
+    """y[M, N] = act(alpha * x[M, K] @ W + bias) + beta * out, through aria_q4_0_matmul_ws.
+
+    activation: None, or "gelu" for the reference's tanh-form GELU fused into the
+    epilogue (its add_bias + gelu_fwd after ffn_up, src/transformer_cuda.rs:1789-1794).
 
     const_weights: the weight buffer is not written by the kernel preceding this
     call on the stream (model weights), so the kernel may start reading it early.
@@ -191,7 +196,8 @@ def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bia
          bias.data_ptr() if bias is not None else None, float(alpha), float(beta),
          workspace.data_ptr() if workspace is not None else None,
          workspace.numel() * workspace.element_size() if workspace is not None else 0,
-         (_lib.FLAG_CONST_WEIGHTS if const_weights else 0) | _KERNEL_FLAGS[kernel], _stream(x.device))
+         (_lib.FLAG_CONST_WEIGHTS if const_weights else 0) | _KERNEL_FLAGS[kernel] | _ACT_FLAGS[activation],
+         _stream(x.device))
     return out
 
 

@@ -123,7 +123,13 @@ enum {
   ARIA_Q4_FLAG_KERNEL_STREAM = 2,
   ARIA_Q4_FLAG_KERNEL_REGISTER = 4,
   /* TENSOR: the tcgen05 tensor-core kernel (any M >= 1). */
-  ARIA_Q4_FLAG_KERNEL_TENSOR = 8
+  ARIA_Q4_FLAG_KERNEL_TENSOR = 8,
+  /* Epilogue activation: y = gelu(alpha * x.W + bias) + beta * y, with the
+   * reference's tanh-form GELU computed in f32 and one rounding to y's type.
+   * Replaces the reference's add_bias + gelu_fwd launches after the ffn_up
+   * projection (src/transformer_cuda.rs:1789-1794, src/kernels.cu:574-583),
+   * which round to f16 after the GEMM, the bias add and the GELU. */
+  ARIA_Q4_FLAG_EPILOGUE_GELU = 16
 };
 
 /* aria_q4_0_matmul with scheduling flags (ARIA_Q4_FLAG_*); flags = 0 is exactly

@@ -108,6 +108,13 @@ def matmul_ref(blocks, layout: int, K: int, N: int, x_f16, bias_f16=None, alpha:
     return y
 
 
+def gelu_tanh(y) -> np.ndarray:
+    """GELU in its tanh form, fp64, as the reference's gelu_fwd states it
+    (lold3344/ARIA src/kernels.cu:574-583): 0.5 y (1 + tanh(0.7978845608 (y + 0.044715 y^3)))."""
+    y = np.asarray(y, dtype=np.float64)
+    return 0.5 * y * (1.0 + np.tanh(0.7978845608 * (y + 0.044715 * y ** 3)))
+
+
 # ------------------------------------------------------------ C oracle binding
 
 def build_c_oracle() -> str:

@@ -73,9 +73,11 @@ def check_close(y, ref, max_abs=1e-2, rel_l2=1e-3, what=""):
 
 
 def run_projection(q4, coracle, layout, K, N, M, out_dtype=None, bias=False, alpha=1.0, beta=0.0, seed=0,
-                   wscale=0.02, ldx=None, flags=0):
+                   wscale=0.02, ldx=None, flags=0, gelu=False):
     """One aria_q4_0_matmul call on seeded inputs, checked for canary damage;
-    returns (y, fp64 reference).  ldx > K leaves a gap after each x row."""
+    returns (y, fp64 reference).  ldx > K leaves a gap after each x row.  gelu:
+    request the GELU epilogue (ARIA_Q4_FLAG_EPILOGUE_GELU) and apply it to the
+    reference before the beta term."""
     import torch
     if out_dtype is None:
         out_dtype = torch.float32
@@ -87,6 +89,10 @@ def run_projection(q4, coracle, layout, K, N, M, out_dtype=None, bias=False, alp
     b = (rng.standard_normal(N) * 0.1).astype(np.float16) if bias else None
     blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
     ref = coracle.matmul_ref(blocks, layout, K, N, x, b, alpha)
+    if gelu:
+        from oracle.q4_oracle_np import gelu_tanh
+        ref = gelu_tanh(ref)
+        flags |= 16  # ARIA_Q4_FLAG_EPILOGUE_GELU
     wq = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
     # canaries: extra rows and columns around the output must stay untouched
     ldy = N + 8

@@ -89,4 +89,7 @@ def test_kernel_choice_routing():
     assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 2 | 4) == -1       # two kernels requested
     assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 8) == TENSOR
     assert L.aria_q4_0_kernel_choice(KN, 896, 48, 1, 0, 0) == -2            # KN needs N % 32 == 0
+    for M in (1, 16, 4096):  # the GELU epilogue flag does not change the routing
+        assert L.aria_q4_0_kernel_choice(KN, 896, 3584, M, 0, 16) == L.aria_q4_0_kernel_choice(KN, 896, 3584, M, 0, 0)
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 32) == -1          # unknown flag
 

@@ -179,5 +179,36 @@ def test_matmul_ex_rejects_unknown_flags(q4):
     x = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
     y = torch.zeros(1, 64, dtype=torch.float16, device="cuda")
     rc = lib().aria_q4_0_matmul_ex(w.buf.data_ptr(), 0, 64, 64, x.data_ptr(), 1, 64, y.data_ptr(), 1, 64, None,
-                                   1.0, 0.0, 16, None)
+                                   1.0, 0.0, 32, None)
     assert rc == 1
+
+
+# (kernel flag, layout, K, N, M): every kernel's epilogue, tensor-core cases with
+# and without a K split through the workspace
+GELU_CASES = [(2, LAYOUT_NK, 4096, 1001, 1), (2, LAYOUT_KN, 3584, 896, 8), (4, LAYOUT_KN, 896, 3584, 4),
+              (4, LAYOUT_NK, 896, 1001, 32), (8, LAYOUT_KN, 896, 2688, 300), (8, LAYOUT_NK, 3584, 896, 64)]
+
+
+@pytest.mark.parametrize("kflag,layout,K,N,M", GELU_CASES)
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_gelu_epilogue(q4, coracle, kflag, layout, K, N, M, out_dtype):
+    """ARIA_Q4_FLAG_EPILOGUE_GELU: y = gelu(alpha x.W + bias) + beta y against the
+    fp64 reference with the reference's tanh-form GELU (src/kernels.cu:574-583)."""
+    y, ref = run_projection(q4, coracle, layout, K, N, M, out_dtype=out_dtype, bias=True, alpha=0.75, beta=0.5,
+                            flags=kflag, gelu=True, wscale=0.05)
+    check_close(y, ref, what=f"gelu kernel={kflag} {layout} {K}x{N} M={M}")
+
+
+def test_gelu_python_mirror(q4, coracle):
+    """q4.matmul(..., activation="gelu") through the auto workspace (split K)."""
+    from oracle.q4_oracle_np import gelu_tanh
+    from aria_b200.efkolos import synth_f16
+    K, N, M = 3584, 896, 64
+    w16 = synth_f16((K, N), 0.05, 31)
+    wq = q4.Q4Weight.from_f16(w16, LAYOUT_KN)
+    x = synth_f16((M, K), 1.0, 32)
+    b = synth_f16((N,), 0.1, 33)
+    y = q4.matmul(x, wq, bias=b, out_dtype=torch.float32, activation="gelu")
+    blocks = coracle.quantize_q4_0_f16(w16.cpu().numpy().reshape(-1))
+    ref = gelu_tanh(coracle.matmul_ref(blocks, LAYOUT_KN, K, N, x.cpu().numpy(), b.cpu().numpy(), 1.0))
+    check_close(y.cpu().numpy(), ref, what="q4.matmul gelu")

@@ -95,3 +95,17 @@ def test_baseline_projection_matches_reference(coracle):
         coracle.baseline_projection(blocks, layout, K, N, x, ws, xs, y, 2)
         ref = coracle.matmul_ref(blocks, layout, K, N, x)
         np.testing.assert_allclose(y, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_gelu_tanh_restatement():
+    """The oracle's GELU is the reference's tanh form (src/kernels.cu:574-583)."""
+    import math
+    from oracle.q4_oracle_np import gelu_tanh
+    xs = np.array([-6.0, -3.0, -1.0, -0.5, 0.0, 0.25, 1.0, 2.0, 8.0])
+    want = [0.5 * v * (1.0 + math.tanh(0.7978845608 * (v + 0.044715 * v ** 3))) for v in xs]
+    assert np.allclose(gelu_tanh(xs), want, rtol=0, atol=1e-15)
+    assert gelu_tanh(0.0) == 0.0 and abs(gelu_tanh(8.0) - 8.0) < 1e-12 and abs(gelu_tanh(-8.0)) < 1e-12
+    # within 1e-3 of the exact erf GELU over [-4, 4] (the approximation's published accuracy)
+    grid = np.linspace(-4, 4, 801)
+    exact = np.array([0.5 * v * (1.0 + math.erf(v / math.sqrt(2.0))) for v in grid])
+    assert np.max(np.abs(gelu_tanh(grid) - exact)) < 1e-3
