@@ -5,24 +5,24 @@
 // lold3344/ARIA src/transformer_cuda.rs:615-640; call sites :1583 QKV, :1686
 // attn_out, :1753 ffn_up, :1805 ffn_down, :1864 LM head).  The product is bound
 // by weight bytes (0.5625 B per weight), so the kernel is built around keeping
-// enough of them in flight on every SM:
+// enough of them in flight on every SM and dequantising them at that rate:
 //
 //  * Persistent grid: two CTAs (8 warps each) per SM when their shared memory
 //    allows, else one; or clusters of C CTAs when the weight has few row tiles
-//    and a tall K.  A cluster owns a contiguous range of row tiles (16*R output
+//    and a tall K.  Cluster q owns row tiles q, q + clusters, ... (16*R output
 //    features each); its C CTAs split K, and the 8 warps of a CTA split the
 //    CTA's K range again.
 //  * Every warp streams its own sequence of (row tile, 128-k group) chunks --
-//    16*R rows x 64 bytes of codes plus that chunk's scales -- through a private
-//    ring of 6/R shared-memory stages with 16-byte cp.async copies (about 55-61
-//    KB in flight per CTA).  The ring runs across tile boundaries, so the stream
+//    16*R rows x 64*P bytes of codes plus that chunk's scales -- through a
+//    private ring of 6/(R*P) stages (2 when R*P = 4) with 16-byte cp.async
+//    copies (55-74 KB of ring per CTA).  The ring runs across tile boundaries, so the stream
 //    never drains until the CTA's last chunk.  No register is spent on bytes in
 //    flight, and waiting is cp.async.wait_group on the warp's own copies: no
 //    spin loop anywhere.
 //  * The activations of the CTA's K range are staged once in shared memory.
 //  * Maths as in the register-fed kernel: codes become exact (q-8) f16x2 values
-//    with LOP3 + HSUB/HFMA, and feed m16n8k16 tensor-core MMAs (A = weights, B =
-//    activations, f32 accumulation).  NK scales: each 32-k block's MMA pair
+//    with LOP3 + HSUB/HFMA, written straight into the A-fragment order of
+//    m16n8k16 tensor-core MMAs (A = weights, B = activations, f32 accumulation).  NK scales: each 32-k block's MMA pair
 //    starts from zero and is scaled in f32 (exact products, f32 sums).  KN scales
 //    are folded into the activation fragment (x*s rounded to f16).
 //  * Partial sums: after each row tile, every warp deposits its fragment in a
@@ -580,9 +580,9 @@ static int gemv_max_clusters(int layout, int R, int P, int C, int per_sm, int sm
 //   + 20 per token row and 128-k group of activations staged per SM (the
 //     prologue copies them from L2 before the weight stream starts)
 //   + 3000 for a cluster split (cluster barriers, distributed-shared-memory sums).
-// The kernel is bound by how fast its few chunks per warp arrive rather than by
-// arithmetic (dropping all arithmetic leaves the time unchanged), hence the large
-// per-chunk term.
+// Time is set by each warp's chain of chunk arrival -> dequantisation -> MMA ->
+// scale FMAs (without the arithmetic the same copies stream ~1.8x faster), so the
+// terms count a warp's chunks and blocks rather than bytes.
 static bool plan_gemv(int layout, int K, int N, int M, int sms, GemvPlan& best) {
   const int KG = padded_k(K) / 128;
   long long best_cost = -1;
