@@ -120,10 +120,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // with four slots in all)
   // NACC = 2 accumulators let the next tile's MMAs overlap this tile's
   // epilogue; NACC = 1 leaves TMEM room for token tiles up to 256 (for shapes
-  // whose tiles fit one round of CTAs there is no next tile to overlap).
+  // whose tiles fit one round of CTAs there is no next tile to overlap).  With
+  // BT = 192 and NACC = 2 one A slot per warpgroup remains: a warpgroup then
+  // dequantises group G + 2 while the MMAs of the other warpgroup's group G + 1
+  // run, which at 192 tokens take longer than the dequantisation.
   constexpr int kFreeCols = 512 - NACC * BT;
   constexpr int kASlots = kFreeCols / kAStageCols >= 8 ? 8 : (kFreeCols / kAStageCols) & ~1;
-  static_assert(kASlots >= 4, "two A slots per dequant warpgroup");
+  static_assert(kASlots >= 2, "one A slot per dequant warpgroup at least");
   constexpr int kAPer = kASlots / 2;
   constexpr uint32_t kAColBase = NACC * BT;  // A stages follow the accumulators
   constexpr uint32_t kNeed = NACC * BT + kASlots * kAStageCols;
@@ -605,7 +608,7 @@ static int tc_num_sms() {
 }
 
 struct TcPlan {
-  int bt = 64, splits = 1;
+  int bt = 64, nacc = 2, splits = 1;
   size_t ws_bytes = 0;  // workspace the plan needs (0 without split-K)
 };
 
@@ -632,10 +635,13 @@ static size_t tc_ws_bytes(int N, int M, int bt, int splits) {
 // is the MMA issuer's latency (two barrier waits, a fence, eight MMAs and two
 // commits).  K splits are considered for 64- and 128-token tiles, with every
 // slice at least two 128-k groups, when the workspace holds the plan's
-// ws_bytes.
+// ws_bytes.  192-token tiles come with one accumulator (deeper A sub-rings; kept
+// on ties, i.e. when the tiles fit one round) or two (the epilogue overlapped;
+// measured on B200 at M = 4096: Efkolos LM head 255 -> 248 us, config-4
+// ffn_down 508 -> 499 us, where the model picks it).
 static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
   struct Cand { int bt, nacc; };
-  const Cand cands[] = {{64, 2}, {128, 2}, {192, 1}, {224, 1}, {256, 1}};
+  const Cand cands[] = {{64, 2}, {128, 2}, {192, 1}, {224, 1}, {256, 1}, {192, 2}};
   const int splits_c[] = {1, 2, 3, 4, 6, 8};  // the reduction unrolls up to 8 slices
   const long long n_tiles = (N + 127) / 128;
   const int KG = padded_k(K) / 128;
@@ -658,6 +664,7 @@ static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
         best.bt = c.bt;
+        best.nacc = c.nacc;
         best.splits = S;
         best.ws_bytes = need;
       }
@@ -696,7 +703,8 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
     switch (p.bt) {
       case 64: return launch_tc_t<1, 64, 4, 2>(a, x, ldx, st, pdl);
       case 128: return launch_tc_t<1, 128, 3, 2>(a, x, ldx, st, pdl);
-      case 192: return launch_tc_t<1, 192, 3, 1>(a, x, ldx, st, pdl);
+      case 192: return p.nacc == 2 ? launch_tc_t<1, 192, 3, 2>(a, x, ldx, st, pdl)
+                                   : launch_tc_t<1, 192, 3, 1>(a, x, ldx, st, pdl);
       case 224: return launch_tc_t<1, 224, 2, 1>(a, x, ldx, st, pdl);
       default: return launch_tc_t<1, 256, 2, 1>(a, x, ldx, st, pdl);
     }
@@ -704,7 +712,8 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   switch (p.bt) {
     case 64: return launch_tc_t<0, 64, 4, 2>(a, x, ldx, st, pdl);
     case 128: return launch_tc_t<0, 128, 3, 2>(a, x, ldx, st, pdl);
-    case 192: return launch_tc_t<0, 192, 3, 1>(a, x, ldx, st, pdl);
+    case 192: return p.nacc == 2 ? launch_tc_t<0, 192, 3, 2>(a, x, ldx, st, pdl)
+                                 : launch_tc_t<0, 192, 3, 1>(a, x, ldx, st, pdl);
     case 224: return launch_tc_t<0, 224, 2, 1>(a, x, ldx, st, pdl);
     default: return launch_tc_t<0, 256, 2, 1>(a, x, ldx, st, pdl);
   }
