@@ -235,8 +235,11 @@ constexpr int kOutGelu = 2;
 
 // GELU, tanh form, in f32 as the reference's gelu_fwd computes it
 // (lold3344/ARIA src/kernels.cu:574-583): 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
-// (Hendrycks & Gimpel's approximation; tanhf is CUDA's).
-__device__ __forceinline__ float gelu_tanh(float v) {
+// (Hendrycks & Gimpel's approximation; tanhf is CUDA's).  Kept out of line: the
+// epilogues test the flag per element, and an inlined tanhf in the not-taken
+// branch bloated the unrolled store and split-K reduction loops (measured: 9%
+// slower batched decode with the flag off).
+static __device__ __noinline__ float gelu_tanh(float v) {
   const float c = 0.7978845608f;  // sqrt(2 / pi)
   return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
 }
