@@ -5,7 +5,8 @@
 //                         GPU: flat f16/f32 -> 18-byte GGUF blocks, byte-identical.
 //   unpack_aos_kernel     the exact inverse (q-8)*scale, for checking and export.
 //   repack_{nk,kn}_kernel GGUF blocks -> tiled planes (what a Q4_0 GGUF loader
-//                         uploads; the reference has no reader, §0.3 of the survey).
+//                         uploads; the reference's loader reads only f16 tensors,
+//                         src/transformer_cuda.rs:3046-3065).
 //   quantize_tiled_*      f16 weights -> tiled planes directly, sharing the exact
 //                         block quantiser with pack_aos_kernel.
 #include "q4_common.cuh"
