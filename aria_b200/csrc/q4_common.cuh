@@ -236,16 +236,20 @@ constexpr int kOutGelu = 2;
 // GELU, tanh form, in f32 as the reference's gelu_fwd computes it
 // (lold3344/ARIA src/kernels.cu:574-583): 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
 // (Hendrycks & Gimpel's approximation; tanhf is CUDA's).  Kept out of line: the
-// epilogues test the flag per element, and an inlined tanhf in the not-taken
-// branch bloated the unrolled store and split-K reduction loops (measured: 9%
-// slower batched decode with the flag off).
+// tensor-core epilogue tests the flag per element, and an inlined tanhf in the
+// not-taken branch bloated its unrolled store and split-K reduction loops
+// (measured: 9% slower batched decode with the flag off).
 static __device__ __noinline__ float gelu_tanh(float v) {
   const float c = 0.7978845608f;  // sqrt(2 / pi)
   return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
 }
 
+// One output value: [GELU](v) + beta * y, f16 or f32.  The activation is a
+// template argument: callers branch on (ydt & kOutGelu) once, outside their
+// store loops, so the loop without it holds no call.
+template <bool GELU>
 __device__ __forceinline__ void store_out(void* y, int ydt, size_t idx, float v, float beta) {
-  if (ydt & kOutGelu) v = gelu_tanh(v);
+  if (GELU) v = gelu_tanh(v);
   if ((ydt & kOutF16) == 0) {
     float* yp = reinterpret_cast<float*>(y) + idx;
     if (beta != 0.0f) v += beta * *yp;
