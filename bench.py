@@ -151,6 +151,19 @@ def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
                       f"(dequantise + f32 i-p-j matmul, {threads} OpenMP threads)"}
 
 
+def cpu_model() -> str:
+    """Host CPU model name (for the CPU-baseline record)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
@@ -162,6 +175,8 @@ def run_reference(args, rank: int) -> None:
     v = statistics.median([r["value"] for r in vals])
     cb = dict(vals[0])
     cb["value"] = v
+    cb["cpu_model"] = cpu_model()
+    cb["nproc"] = os.cpu_count()
     rec = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -524,6 +539,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_decode_sample(12.0)
+        # the reference's cpu_matmul is serial: also the single-thread rate
+        one = cpu_decode_sample(6.0, threads=1)
+        cpu["single_thread"] = {"value": one["value"], "unit": one["unit"], "cores": 1, "sample": one["sample"]}
+        cpu["cpu_model"] = cpu_model()
+        cpu["nproc"] = os.cpu_count()
 
     rec = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
