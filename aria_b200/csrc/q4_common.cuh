@@ -65,7 +65,9 @@ __host__ __device__ inline int dev_nibble_pos(int i) { return (i >> 1) + 4 * (i 
 // Pack 8 codes (element order) into one device word.
 __host__ __device__ inline uint32_t dev_word_from_codes(const uint8_t* q8) {
   uint32_t w = 0;
+#ifdef __CUDA_ARCH__
 #pragma unroll
+#endif
   for (int i = 0; i < 8; i++) w |= (uint32_t)(q8[i] & 0xF) << (4 * dev_nibble_pos(i));
   return w;
 }

@@ -345,7 +345,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int acnt = 0;  // stages this warpgroup has produced into its A sub-ring
     Cursor dc;
     for (cursor_first(dc, 0); dc.j < my_tiles && ok; cursor_next(dc), seq++) {
-      const int G = dc.G;
       {
         __syncwarp();  // every lane is done reading the slot the next issue overwrites
         issue();
