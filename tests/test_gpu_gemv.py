@@ -44,6 +44,13 @@ PLANS = [
     (LAYOUT_NK, 4096, 1001, 1), (LAYOUT_NK, 4096, 1001, 3), (LAYOUT_NK, 4096, 1001, 8),
     (LAYOUT_NK, 1056, 300, 1), (LAYOUT_NK, 1056, 300, 8),
     (LAYOUT_NK, 896, 31500, 1),
+    # kinds the launch planner reaches on other shapes: 2-CTA clusters holding
+    # several tiles each, 16-row one-group chunks (also single-token NK, and with
+    # 4-CTA clusters), and a warp slice of odd length under two-group chunks
+    (LAYOUT_KN, 10240, 12000, 8), (LAYOUT_NK, 10240, 12000, 8),
+    (LAYOUT_KN, 128, 32, 1), (LAYOUT_NK, 128, 32, 1), (LAYOUT_NK, 128, 32, 3),
+    (LAYOUT_KN, 3072, 32, 8), (LAYOUT_NK, 12288, 32, 1),
+    (LAYOUT_KN, 4608, 32, 1), (LAYOUT_NK, 4608, 32, 1),
 ]
 
 
