@@ -22,8 +22,10 @@ cudaError_t launch_gemv(const uint8_t* tiled, int layout, int K, int N, const __
                         bool const_weights);
 cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                            int ydt, int ldy, const __half* bias, float alpha, float beta, void* workspace,
-                           size_t workspace_bytes, cudaStream_t st, bool pdl);
+                           size_t workspace_bytes, cudaStream_t st, bool pdl,
+                           unsigned long long wait_ns = 1000000000ull, bool no_x_loads = false);
 size_t tc_workspace_bytes(int K, int N, int M);
+size_t tc_workspace_used(int K, int N, int M, size_t ws_avail);
 size_t tc_workspace_counter_bytes();
 int take_device_error();
 }  // namespace aria_q4
@@ -159,9 +161,10 @@ size_t aria_q4_0_workspace_bytes(int K, int N, int M) {
   return tc_workspace_bytes(K, N, M);
 }
 
-int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
-                        int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, void* workspace,
-                        size_t workspace_bytes, int flags, void* stream) {
+// Arguments shared by every projection entry point; ARIA_Q4_OK when a launch
+// may follow (M == 0 also returns ARIA_Q4_OK: the caller then launches nothing).
+static int check_matmul_args(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx,
+                             const void* y, int y_dtype, int ldy, int flags) {
   if (int s = check_tiled_shape(layout, K, N)) return s;
   if (M < 0) return ARIA_Q4_EINVAL;
   if (M == 0) return ARIA_Q4_OK;
@@ -172,6 +175,14 @@ int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint1
                     ARIA_Q4_FLAG_KERNEL_TENSOR | ARIA_Q4_FLAG_EPILOGUE_GELU;
   if ((flags & ~known) != 0) return ARIA_Q4_EINVAL;
   if (((uintptr_t)tiled & 255u) != 0 || !aligned16(x) || (ldx % 8) != 0) return ARIA_Q4_EALIGN;
+  return ARIA_Q4_OK;
+}
+
+int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,
+                        int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta, void* workspace,
+                        size_t workspace_bytes, int flags, void* stream) {
+  if (int s = check_matmul_args(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, flags)) return s;
+  if (M == 0) return ARIA_Q4_OK;
   if (workspace_bytes == 0) workspace = nullptr;
   if (workspace && ((uintptr_t)workspace & 255u) != 0) return ARIA_Q4_EALIGN;
   if (int s = check_device()) return s;
@@ -191,6 +202,8 @@ int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint1
                                     (const __half*)bias, alpha, beta, workspace, workspace_bytes, st, true));
 }
 
+size_t aria_q4_0_workspace_counter_bytes(void) { return tc_workspace_counter_bytes(); }
+
 int aria_q4_0_kernel_choice(int layout, int K, int N, int M, size_t workspace_bytes, int flags) {
   if (int s = check_tiled_shape(layout, K, N)) return -s;
   if (M < 1) return -ARIA_Q4_EINVAL;
@@ -208,12 +221,16 @@ int aria_q4_0_matmul_ex(const void* tiled, int layout, int K, int N, const uint1
 
 // ------------------------------------------------------------------ static-scratch variant
 // Scratch of aria_q4_0_matmul_static_ws: one file-scope device array per
-// device (zero at module load), so the call allocates nothing.
+// device (zero at module load), so the call allocates nothing.  Its first
+// bytes are the split-K counter region, the rest the f32 partials.
 static constexpr size_t kStaticWsBytes = 8u << 20;
 static __device__ __align__(256) unsigned char g_static_ws[kStaticWsBytes];
 
 // Device address of g_static_ws on the current device, looked up once per
-// device; nullptr (and *err set) when the lookup fails.
+// device (the first call on a device, which should therefore come before any
+// stream capture); nullptr (and *err set) when the lookup fails.  The cache
+// assumes the device's context lives as long as the process: after
+// cudaDeviceReset the module, and with it the array, may be reloaded elsewhere.
 static void* static_ws_address(cudaError_t* err) {
   constexpr int kMaxDevices = 64;
   static void* addr[kMaxDevices] = {};
@@ -239,20 +256,38 @@ static void* static_ws_address(cudaError_t* err) {
 int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx,
                                void* y, int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta,
                                int flags, void* stream) {
-  // the workspace the tensor-core kernel's plan would use (only M > 32 splits K)
-  const size_t need = (M > 32 && check_tiled_shape(layout, K, N) == ARIA_Q4_OK) ? tc_workspace_bytes(K, N, M) : 0;
-  if (need > kStaticWsBytes) return ARIA_Q4_ESIZE;
-  void* ws = nullptr;
-  if (need > 0) {
-    cudaError_t e = cudaSuccess;
-    ws = static_ws_address(&e);
-    if (!ws) return cuda_status(e);
-    // the split-K counters must start at zero (a call cut short may leave them set)
-    e = cudaMemsetAsync(ws, 0, tc_workspace_counter_bytes(), (cudaStream_t)stream);
-    if (e != cudaSuccess) return cuda_status(e);
-  }
-  return aria_q4_0_matmul_ws(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, ws, need, flags,
-                             stream);
+  if (int s = check_matmul_args(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, flags)) return s;
+  if (M == 0) return ARIA_Q4_OK;
+  // The kernel and K split the library picks with kStaticWsBytes of workspace:
+  // the tensor-core planner only considers splits whose partials fit, so every
+  // shape runs (with a smaller split, or none, where the best one would not fit).
+  const int kern = choose_kernel(K, N, M, true, flags);
+  if (kern < 0) return -kern;
+  const bool splits = kern == ARIA_Q4_KERNEL_TENSOR && tc_workspace_used(K, N, M, kStaticWsBytes) > 0;
+  if (!splits)
+    return aria_q4_0_matmul_ws(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, nullptr, 0,
+                               flags, stream);
+  cudaError_t e = cudaSuccess;
+  void* ws = static_ws_address(&e);
+  if (!ws) return cuda_status(e);
+  // the split-K counters must start at zero (a call cut short by an expired
+  // bounded wait may leave some set)
+  e = cudaMemsetAsync(ws, 0, tc_workspace_counter_bytes(), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  return aria_q4_0_matmul_ws(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, ws, kStaticWsBytes,
+                             flags, stream);
+}
+
+// ------------------------------------------------------------------ failure-path test hook
+int aria_q4_test_tensor_stall(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx,
+                              void* y, int y_dtype, int ldy, unsigned wait_limit_us, void* stream) {
+  if (int s = check_matmul_args(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, 0)) return s;
+  if (M == 0) return ARIA_Q4_OK;
+  if (wait_limit_us == 0 || wait_limit_us > 1000000u) return ARIA_Q4_EINVAL;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
+                                    nullptr, 1.0f, 0.0f, nullptr, 0, (cudaStream_t)stream, false,
+                                    (unsigned long long)wait_limit_us * 1000ull, true));
 }
 
 int aria_q4_0_matmul(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx, void* y,

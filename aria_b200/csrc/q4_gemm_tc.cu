@@ -56,6 +56,13 @@ struct TcArgs {
   int splits;
   float* ws_part;
   unsigned* ws_cnt;
+  // limit of the MMA issuer's waits (tc::kWaitLimitNs in production); every
+  // other wait (producers, epilogue), which depends on the issuer's progress,
+  // gets twice as long, so a stalled operand stage is reported by the issuer
+  unsigned long long wait_ns;
+  // failure-path test only: the X-tile producer issues no copies, so the MMA
+  // issuer's first wait runs out and the CTA unwinds
+  int no_x_loads;
 };
 
 // K-slice of work unit `unit` in 128-k groups: [g0, g1)
@@ -143,8 +150,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* empty_a = full_a + kASlots;  // [kASlots]
   uint64_t* acc_full = empty_a + kASlots;  // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* mma_drain = acc_empty + 2;     // [1] error path: completion of every issued MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  // A wait that runs out records its code and raises abort_flag; every other
+  // wait of the CTA then returns at once (its phase can no longer complete),
+  // so the CTA unwinds within one wait limit.
+  auto give_up = [&](int wait_result, int code) {
+    if (wait_result == tc::kWaitTimeout) tc::record_error(code);
+    atomicExch(abort_flag, 1);
+  };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int my_tiles = (num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
@@ -162,6 +177,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::mbar_init(&acc_full[b], 1);
       tc::mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
+    tc::mbar_init(mma_drain, 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -180,7 +196,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if (lane == 0 && !a.no_x_loads) {
       int it = 0;
       bool ok = true;
       const int KG = a.Kp >> 7;
@@ -190,10 +206,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int m0 = (tile / n_tiles) * BT;
         for (int G = g0; G < g1; G++, it++) {
           const int s = it % STAGES;
-          if (it >= STAGES && !tc::mbar_wait(&empty_x[s], ((it / STAGES) - 1) & 1)) {
-            tc::record_error(tc::kErrTimeoutEmpty);
-            ok = false;
-            break;
+          if (it >= STAGES) {
+            const int w = tc::mbar_wait_or_abort(&empty_x[s], ((it / STAGES) - 1) & 1, 2 * a.wait_ns, abort_flag);
+            if (w != tc::kWaitOk) {
+              give_up(w, tc::kErrTimeoutEmpty);
+              ok = false;
+              break;
+            }
           }
           // two boxes of 64 k on one barrier (the second may lie past K: zero-filled)
           tc::mbar_arrive_expect_tx(&full_x[s], 2 * L::kXTile);
@@ -223,10 +242,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int j = 0; j < my_tiles && ok; j++) {
         const int buf = NACC == 2 ? (j & 1) : 0;
         const int use = NACC == 2 ? (j >> 1) : j;  // earlier uses of this accumulator
-        if (use >= 1 && !tc::mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
-          tc::record_error(tc::kErrTimeoutAccum);
-          ok = false;
-          break;
+        if (use >= 1) {
+          const int w = tc::mbar_wait_or_abort(&acc_empty[buf], (use - 1) & 1, a.wait_ns, abort_flag);
+          if (w != tc::kWaitOk) {
+            give_up(w, tc::kErrTimeoutAccum);
+            ok = false;
+            break;
+          }
         }
         tc::tc_fence_after();
         const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT);
@@ -242,8 +264,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           } else {
             if (++aslot0 == kAPer) { aslot0 = 0; aph0 ^= 1u; }
           }
-          if (!tc::mbar_wait(&full_x[xslot], xph) || !tc::mbar_wait(&full_a[as], aph)) {
-            tc::record_error(tc::kErrTimeoutFull);
+          int wr = tc::mbar_wait_or_abort(&full_x[xslot], xph, a.wait_ns, abort_flag);
+          if (wr == tc::kWaitOk) wr = tc::mbar_wait_or_abort(&full_a[as], aph, a.wait_ns, abort_flag);
+          if (wr != tc::kWaitOk) {
+            give_up(wr, tc::kErrTimeoutFull);
             ok = false;
             break;
           }
@@ -262,7 +286,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc::umma_commit(&acc_full[buf]);  // also on the error path, so the epilogue is released
       }
-      if (!ok) atomicExch(abort_flag, 1);
+      if (!ok) {
+        // no MMA issued by this thread may still write tensor memory when the CTA
+        // frees it: wait (bounded) for all of them
+        tc::umma_commit(mma_drain);
+        tc::mbar_wait(mma_drain, 0);
+      }
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------ dequantisers
@@ -361,10 +390,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int c = acnt++;
         const int s = wg * kAPer + c % kAPer;  // A slot in this warpgroup's sub-ring
         // warp-uniform outcome: tcgen05.st and the per-warp arrival below are warp-collective
-        if (c >= kAPer && !__all_sync(0xffffffffu, tc::mbar_wait(&empty_a[s], ((c / kAPer) - 1) & 1))) {
-          tc::record_error(tc::kErrTimeoutEmpty);
-          ok = false;
-          break;
+        if (c >= kAPer) {
+          const int w = tc::mbar_wait_or_abort(&empty_a[s], ((c / kAPer) - 1) & 1, 2 * a.wait_ns, abort_flag);
+          const bool all_ok = __all_sync(0xffffffffu, w == tc::kWaitOk);
+          const bool any_timeout = __any_sync(0xffffffffu, w == tc::kWaitTimeout);
+          if (!all_ok) {
+            if (lane == 0) give_up(any_timeout ? tc::kWaitTimeout : tc::kWaitAborted, tc::kErrTimeoutEmpty);
+            ok = false;
+            break;
+          }
         }
 #pragma unroll
         for (int h = 0; h < 2; h++) {
@@ -406,7 +440,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
     cp_async_wait<0>();  // no copy into shared memory may outlive the loop
-    if (!ok) atomicExch(abort_flag, 1);
   } else {
     // ------------------------------------------------------------ epilogue (warps 10..13)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -435,9 +468,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int n = (tile % n_tiles) * 128 + rr;
       const int m0 = (tile / n_tiles) * BT;
       // warp-uniform decisions: the per-warp arrival below is reached by all lanes or none
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&acc_full[buf], use & 1))) {
-        tc::record_error(tc::kErrTimeoutAccum);
-        break;
+      {
+        const int w = tc::mbar_wait_or_abort(&acc_full[buf], use & 1, 2 * a.wait_ns, abort_flag);
+        const bool all_ok = __all_sync(0xffffffffu, w == tc::kWaitOk);
+        const bool any_timeout = __any_sync(0xffffffffu, w == tc::kWaitTimeout);
+        if (!all_ok) {
+          if (lane == 0) give_up(any_timeout ? tc::kWaitTimeout : tc::kWaitAborted, tc::kErrTimeoutAccum);
+          break;
+        }
       }
       if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abort_flag) != 0)) break;
       tc::tc_fence_after();
@@ -536,6 +574,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
+constexpr int kTcMaxDevices = 64;
+
+// SM count of the current device (cached per device).
+static int tc_num_sms() {
+  static int sms[kTcMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kTcMaxDevices) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (sms[dev] <= 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    sms[dev] = n;
+  }
+  return sms[dev];
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -567,19 +626,19 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   auto kern = gemm_tc_kernel<LAYOUT, BT, STAGES, NACC>;
-  static bool attr_set = false;  // idempotent; a racing second set is harmless
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+  // the shared-memory opt-in is a per-device property of the kernel: set it once
+  // on every device this instance runs on (idempotent; a racing second set is harmless)
+  static bool attr_set[kTcMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kTcMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set[dev] = true;
   }
-  static int num_sms = 0;
-  if (num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (num_sms <= 0) num_sms = 148;
-  }
+  const int num_sms = tc_num_sms();
   const int n_tiles = (a.N + 127) / 128;
   const int num_tiles = n_tiles * ((a.M + BT - 1) / BT) * a.splits;  // work units
   cudaLaunchConfig_t cfg = {};
@@ -593,17 +652,6 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, tm, a, n_tiles, num_tiles);
-}
-
-static int tc_num_sms() {
-  static int num_sms = 0;
-  if (num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (num_sms <= 0) num_sms = 148;
-  }
-  return num_sms;
 }
 
 struct TcPlan {
@@ -676,16 +724,27 @@ size_t tc_workspace_bytes(int K, int N, int M) {
   return plan_tc(K, N, M, tc_num_sms(), (size_t)-1).ws_bytes;
 }
 
+// Workspace bytes the launcher's plan uses when ws_avail bytes are available
+// (0: that plan does not split K).
+size_t tc_workspace_used(int K, int N, int M, size_t ws_avail) {
+  return plan_tc(K, N, M, tc_num_sms(), ws_avail).ws_bytes;
+}
+
 // Bytes at the start of a workspace that hold the split-K counters.
 size_t tc_workspace_counter_bytes() { return kTcCounterBytes; }
 
 // Tensor-core projection (prefill, and batched decode above 32 tokens).
 // workspace: optional (nullptr / 0 bytes: no K split); its counter region must
 // be zero before the first use and every call leaves it zero.
+// wait_ns / no_x_loads: see TcArgs (the failure-path test hook passes a short
+// limit and no X copies; every other caller the defaults).
 cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                            int ydt, int ldy, const __half* bias, float alpha, float beta, void* workspace,
-                           size_t workspace_bytes, cudaStream_t st, bool pdl) {
+                           size_t workspace_bytes, cudaStream_t st, bool pdl, unsigned long long wait_ns,
+                           bool no_x_loads) {
   TcArgs a;
+  a.wait_ns = wait_ns;
+  a.no_x_loads = no_x_loads ? 1 : 0;
   a.qs = tiled;
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
   a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;

@@ -68,6 +68,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// Outcome of a pipeline wait inside a CTA that may give up.
+enum : int { kWaitOk = 0, kWaitTimeout = 1, kWaitAborted = 2 };
+
+// Waits for the phase with the given parity for at most limit_ns; returns
+// kWaitAborted as soon as *abort is set (another warp of the CTA gave up first,
+// so this wait can never complete), kWaitTimeout when the limit runs out.
+__device__ __forceinline__ int mbar_wait_or_abort(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                  const volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return kWaitOk;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort != 0) return kWaitAborted;
+    if (globaltimer() - t0 > limit_ns) return kWaitTimeout;
+  }
+  return kWaitOk;
+}
+
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_device_error, 0, code); }
 
 // 2-D tiled TMA load into this CTA's shared memory, completion on `bar`.

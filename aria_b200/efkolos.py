@@ -99,31 +99,43 @@ class Q4Stack:
 
 
 class DecodeProgram:
-    """The ordered projection chain of one decode step over preallocated buffers.
+    """One decode (or prefill) step's chain of projections over preallocated buffers.
 
-    Each projection reads its own activation buffer x_i [M, K] and writes y_i
-    [M, N] (f16, the reference's activation dtype).  The ops between projections
-    are out of scope; the launch order is the model's, and every launch waits for
-    the previous one on the stream (programmatic dependent launch), as a real
-    decode step's data dependencies require."""
+    The data flow follows the reference's layer (src/transformer_cuda.rs:1059-1166
+    and forward_gpu :1583-:1864): the residual stream h [M, d] feeds QKV; attn_out
+    adds into h (the reference's residual add, fused as beta = 1); h feeds ffn_up,
+    whose GELU is fused into its epilogue; ffn_down adds into h; after the last
+    layer h feeds the LM head.  Attention and LayerNorm are outside this library:
+    attn_out reads the first d_model columns of the QKV output in place of the
+    attention output, and h is not normalised.  Every projection therefore
+    consumes the output of the one before it, and every launch waits for the
+    previous one on the stream (programmatic dependent launch) before it reads
+    its activations.  A step starts by copying the input h0 into h."""
 
     def __init__(self, stack: Q4Stack, M: int, device="cuda", seed: int = 1):
+        cfg = stack.cfg
         self.stack = stack
         self.M = M
-        # all inputs live in one buffer so a host->device refresh is a single copy
-        sizes = [M * w.K for _, w in stack.weights]
-        self.x_all = synth_f16((sum(sizes),), 1.0, seed * 7919, device)
-        self.xs, self.ys = [], []
-        off = 0
-        for (name, w), n in zip(stack.weights, sizes):
-            self.xs.append(self.x_all[off:off + n].view(M, w.K))
-            self.ys.append(torch.empty((M, w.N), dtype=torch.float16, device=device))
-            off += n
+        d = cfg.d_model
+        self.h0 = synth_f16((M, d), 1.0, seed * 7919, device)
+        self.h = torch.empty(M, d, dtype=torch.float16, device=device)
+        self.y_qkv = torch.empty(M, 3 * d, dtype=torch.float16, device=device)
+        self.u = torch.empty(M, cfg.ffn_dim, dtype=torch.float16, device=device)
+        self.logits = torch.empty(M, cfg.vocab_size, dtype=torch.float16, device=device)
 
     def run(self, stack: Q4Stack | None = None) -> None:
         st = stack or self.stack
-        for (name, w), x, y in zip(st.weights, self.xs, self.ys):
-            matmul(x, w, y, const_weights=True)  # model weights: never written inside a step
+        d = st.cfg.d_model
+        w = [q for _, q in st.weights]
+        self.h.copy_(self.h0)
+        for i in range(st.cfg.num_layers):
+            qkv, out, up, down = w[4 * i:4 * i + 4]
+            # model weights are never written inside a step: const-weights flag
+            matmul(self.h, qkv, self.y_qkv, const_weights=True)
+            matmul(self.y_qkv[:, :d], out, self.h, beta=1.0, const_weights=True)
+            matmul(self.h, up, self.u, activation="gelu", const_weights=True)
+            matmul(self.u, down, self.h, beta=1.0, const_weights=True)
+        matmul(self.h, w[-1], self.logits, const_weights=True)
 
     @property
     def launches(self) -> int:
@@ -137,4 +149,7 @@ class DecodeProgram:
         return b
 
     def input_bytes(self) -> int:
-        return self.x_all.numel() * 2
+        return self.h0.numel() * 2
+
+    def output_bytes(self) -> int:
+        return self.logits.numel() * 2

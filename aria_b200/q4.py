@@ -168,12 +168,15 @@ def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bia
     workspace: "auto" (a cached per-device/stream buffer sized by
     aria_q4_0_workspace_bytes), None (no K split) or a zero-initialised uint8
     CUDA tensor owned by the caller."""
-    _require_cuda(x, "x")
+    if not x.is_cuda:
+        raise ValueError("x must be a CUDA tensor")
     if x.dtype != torch.float16:
         raise TypeError("x must be f16 (the reference's activation dtype)")
     x2 = x.reshape(-1, x.shape[-1])
     if x2.shape[1] != w.K:
         raise ValueError(f"x has K={x2.shape[1]}, weight has K={w.K}")
+    if x2.stride(1) != 1:
+        raise ValueError("x rows must be contiguous (a row stride of ldx >= K elements is allowed)")
     M = x2.shape[0]
     if out is None:
         out = torch.empty((M, w.N), dtype=out_dtype, device=x.device)

@@ -4,22 +4,34 @@
 N(0, 0.02) weights (x 1/sqrt(64) for attn_out and ffn_down), Q4_0-packed on the
 device.  Two programs:
 
-* `ColumnSplitDecode` -- decode at batch 64 with ffn_up, ffn_down and the LM
-  head column-split across the ranks (each rank quantises only its slice) and
-  an NCCL all-gather reassembling every split output, which the next split
-  projection consumes (ffn_up -> ffn_down); QKV and attn_out are replicated.
+* `ColumnSplitDecode` -- decode at batch 64.  QKV and attn_out are replicated;
+  ffn_up is column-split across the ranks (its GELU fused into the epilogue)
+  and ffn_down is split along K with the same ranges, so each rank multiplies
+  the ffn_up slice it produced by its rows of ffn_down and one NCCL all-reduce
+  per layer sums the partial products into the residual stream.  The LM head is
+  column-split (vocabulary rows of `embed`) and all-gathered once per step.
+  Each rank quantises only its slices.
 * batch-sharded prefill -- every rank holds the full replica and runs its own
   sequences (aria_b200.efkolos.DecodeProgram over the SCALED config).
+
+The data flow between projections follows the reference's layer
+(lold3344/ARIA src/transformer_cuda.rs:1059-1166): the residual stream h feeds
+QKV and ffn_up, attn_out and ffn_down add into h.  Attention and LayerNorm are
+outside this library: attn_out reads the first d_model columns of the QKV
+output in place of the attention output, and h is not normalised.
 """
 from __future__ import annotations
 
 import math
 
 import torch
+import torch.distributed as dist
 
 from . import dist as adist
 from .efkolos import SCALED, EfkolosConfig, synth_f16
 from .q4 import LAYOUT_KN, LAYOUT_NK, Q4Weight, matmul
+
+FFN_ALIGN = 128  # ffn_up column / ffn_down row ranges: whole 128-k groups of the device layout
 
 
 class ColumnSplitDecode:
@@ -33,55 +45,67 @@ class ColumnSplitDecode:
             base = seed * 1000003 + 10 * i
             qkv = Q4Weight.from_f16(synth_f16((d, 3 * d), s, base + 1, device), LAYOUT_KN)
             out = Q4Weight.from_f16(synth_f16((d, d), sd, base + 2, device), LAYOUT_KN)
-            up_s = adist.ColumnSplit(LAYOUT_KN, d, ff, world, rank)
-            dn_s = adist.ColumnSplit(LAYOUT_KN, ff, d, world, rank)
+            up_s = adist.ColumnSplit(LAYOUT_KN, d, ff, world, rank, align_to=FFN_ALIGN)
+            dn_s = adist.RowSplit(LAYOUT_KN, ff, d, world, rank, align=FFN_ALIGN)
+            assert up_s.cols == dn_s.rows
             # the full tensor is generated identically on every rank; each quantises its slice
-            up = Q4Weight.from_f16(up_s.slice_weight(synth_f16((d, ff), s, base + 3, device)), LAYOUT_KN)
-            dn = Q4Weight.from_f16(dn_s.slice_weight(synth_f16((ff, d), sd, base + 4, device)), LAYOUT_KN)
-            self.layers.append((qkv, out, (up, up_s), (dn, dn_s)))
+            up = dn = None
+            if up_s.cols[1] > up_s.cols[0]:
+                up = Q4Weight.from_f16(up_s.slice_weight(synth_f16((d, ff), s, base + 3, device)), LAYOUT_KN)
+                dn = Q4Weight.from_f16(dn_s.slice_weight(synth_f16((ff, d), sd, base + 4, device)), LAYOUT_KN)
+            self.layers.append((qkv, out, up, dn))
+        self.up_cols = adist.ColumnSplit(LAYOUT_KN, d, ff, world, rank, align_to=FFN_ALIGN).cols
         self.head_s = adist.ColumnSplit(LAYOUT_NK, d, V, world, rank)
         self.head = Q4Weight.from_f16(self.head_s.slice_weight(synth_f16((V, d), s, seed * 1000003 + 7, device)),
                                       LAYOUT_NK)
-        # activations: attention/LayerNorm/GELU are out of scope, so the inputs of
-        # QKV and attn_out are synthetic; ffn_down consumes the gathered ffn_up output
-        self.x = synth_f16((M, d), 1.0, seed + 5, device)
+        self.h0 = synth_f16((M, d), 1.0, seed + 5, device)  # the step's input residual stream
+        self.h = torch.empty(M, d, dtype=torch.float16, device=device)
         self.y_qkv = torch.empty(M, 3 * d, dtype=torch.float16, device=device)
-        self.y_out = torch.empty(M, d, dtype=torch.float16, device=device)
-        self.y_up_l = torch.empty(M, up_s.cols[1] - up_s.cols[0], dtype=torch.float16, device=device)
-        self.y_up = torch.empty(M, ff, dtype=torch.float16, device=device)
-        self.y_dn_l = torch.empty(M, dn_s.cols[1] - dn_s.cols[0], dtype=torch.float16, device=device)
-        self.y_dn = torch.empty(M, d, dtype=torch.float16, device=device)
+        self.u = torch.empty(M, max(1, self.up_cols[1] - self.up_cols[0]), dtype=torch.float16, device=device)
+        self.part = torch.empty(M, d, dtype=torch.float32, device=device)
         self.logits_l = torch.empty(M, self.head_s.cols[1] - self.head_s.cols[0], dtype=torch.float16, device=device)
         self.logits = torch.empty(M, V, dtype=torch.float16, device=device)
 
-    def gather(self, y_local, N, align, out):
-        if self.world == 1:
-            out.copy_(y_local)
-        else:
-            adist.gather_columns(y_local, N, self.world, align, self.group, out=out)
-
     def run(self) -> None:
-        cfg = self.cfg
-        for (qkv, out, (up, up_s), (dn, dn_s)) in self.layers:
-            matmul(self.x, qkv, self.y_qkv, const_weights=True)
-            matmul(self.x, out, self.y_out, const_weights=True)
-            matmul(self.x, up, self.y_up_l, const_weights=True)
-            self.gather(self.y_up_l, cfg.ffn_dim, up_s.align, self.y_up)
-            matmul(self.y_up, dn, self.y_dn_l, const_weights=True)
-            self.gather(self.y_dn_l, cfg.d_model, dn_s.align, self.y_dn)
-        matmul(self.y_dn, self.head, self.logits_l, const_weights=True)
-        self.gather(self.logits_l, cfg.vocab_size, self.head_s.align, self.logits)
+        d = self.cfg.d_model
+        self.h.copy_(self.h0)
+        for (qkv, out, up, dn) in self.layers:
+            matmul(self.h, qkv, self.y_qkv, const_weights=True)
+            matmul(self.y_qkv[:, :d], out, self.h, beta=1.0, const_weights=True)
+            if self.world == 1:
+                matmul(self.h, up, self.u, activation="gelu", const_weights=True)
+                matmul(self.u, dn, self.h, beta=1.0, const_weights=True)
+                continue
+            if up is not None:
+                matmul(self.h, up, self.u, activation="gelu", const_weights=True)
+                matmul(self.u, dn, self.part, out_dtype=torch.float32, const_weights=True)
+            else:
+                self.part.zero_()
+            dist.all_reduce(self.part, group=self.group)  # sum of the ranks' ffn_down partials (f32)
+            self.h.add_(self.part)  # residual add, rounded once to f16
+        matmul(self.h, self.head, self.logits_l, const_weights=True)
+        if self.world == 1:
+            self.logits.copy_(self.logits_l)
+        else:
+            adist.gather_columns(self.logits_l, self.cfg.vocab_size, self.world, self.head_s.align, self.group,
+                                 out=self.logits)
 
     def weight_bytes(self) -> int:
         """Q4_0 bytes this rank streams per step."""
-        b = sum(q.nbytes + o.nbytes + u.nbytes + d.nbytes for (q, o, (u, _), (d, _)) in self.layers)
+        b = 0
+        for (q, o, u, dn) in self.layers:
+            b += q.nbytes + o.nbytes + (u.nbytes + dn.nbytes if u is not None else 0)
         return b + self.head.nbytes
 
-    def gathered_bytes(self) -> int:
-        """Bytes this rank receives from its peers per step through the all-gathers."""
+    def collective_bytes(self) -> int:
+        """Bytes each rank contributes to the collectives per step: one f32
+        [M, d_model] all-reduce per layer and the f16 logits slice's all-gather."""
         if self.world == 1:
             return 0
         cfg = self.cfg
-        f = (self.world - 1) / self.world
-        per_layer = self.M * (cfg.ffn_dim + cfg.d_model) * 2
-        return int(f * (cfg.num_layers * per_layer + self.M * cfg.vocab_size * 2))
+        W = adist.col_width(cfg.vocab_size, self.world, self.head_s.align)
+        return cfg.num_layers * self.M * cfg.d_model * 4 + self.M * W * 2
+
+    @property
+    def collectives_per_step(self) -> int:
+        return 0 if self.world == 1 else self.cfg.num_layers + 1

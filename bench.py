@@ -5,21 +5,27 @@
 
 Workload: one Efkolos decode step at batch 1 -- the
 81 Q4_0 projections of a token (20 layers x QKV 896->2688, attn_out 896->896,
-ffn_up 896->3584, ffn_down 3584->896, plus the LM head 896->31500), launched in
-model order through the C ABI, each waiting on the previous (programmatic
-dependent launch), captured once in a CUDA graph per weight replica.  Metric:
-algorithmic HBM GB/s = (Q4_0 weight bytes + f16 activations in + f16 outputs
-out) / step time.  The weight set (124 MB) is as large as B200's L2, so steps
-rotate over weight replicas totalling > 4x L2; inputs are therefore never
-L2-resident between timed steps.
+ffn_up 896->3584, ffn_down 3584->896, plus the LM head 896->31500) in model
+order with the reference layer's data flow (the residual stream feeds QKV and
+ffn_up, attn_out and ffn_down add into it, GELU after ffn_up), each projection
+consuming the previous one's output; launched through the C ABI, each waiting
+on the previous (programmatic dependent launch), captured once in a CUDA graph
+per weight replica.  Metric: algorithmic HBM GB/s = (Q4_0 weight bytes + f16
+activations in + f16 outputs out) / step time.  The weight set (124 MB) is as
+large as B200's L2, so steps rotate over weight replicas totalling > 4x L2;
+inputs are therefore never L2-resident between timed steps.
 
 Under torchrun (N > 1) every rank decodes its own sequence on a full weight
 replica (batch-sharded weak scaling, no data-path collective); value = bytes
 all ranks streamed / max-over-ranks time.
 
---impl reference times the reference's CPU arithmetic for the same workload
-(dequantise + f32 matmul, the oracle restatement of transformer_cuda.rs:549-575
-and :3322-3333) on the host cores, rank 0 only.
+--impl reference times the reference's CPU arithmetic on the same workload:
+the whole 81-projection step, chained the same way, each projection a
+dequantise + f32 i-p-j matmul (the oracle restatement of
+transformer_cuda.rs:549-575 and :3322-3333), on all host cores, rank 0 only.
+
+--case NAME runs a single projection kind a few times (for ncu captures) and,
+with --time, times it over weight copies larger than 4x L2.
 """
 from __future__ import annotations
 
@@ -51,6 +57,13 @@ def parse():
     ap.add_argument("--batched", type=lambda v: [int(t) for t in v.split(",") if t], default=[16, 64, 256])
     ap.add_argument("--scaled", type=int, default=1, help="1: also run BASELINE configs[4] (d_model 4096)")
     ap.add_argument("--scaled-prefill-tokens", type=int, default=4096)
+    ap.add_argument("--case", default=None,
+                    help="single projection kind (qkv, attn_out, ffn_up, ffn_down, lm_head; prefix scaled_ for "
+                         "BASELINE configs[4]) instead of the benchmark")
+    ap.add_argument("--M", type=int, default=1, help="--case: token rows")
+    ap.add_argument("--launches", type=int, default=3, help="--case: launches before exiting")
+    ap.add_argument("--kernel", default="auto", help="--case: auto, stream, register or tensor")
+    ap.add_argument("--time", action="store_true", help="--case: also time the kind over weight copies")
     return ap.parse_args()
 
 
@@ -116,39 +129,83 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ CPU baseline
 
-def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
-    """The reference's CPU arithmetic on a bounded sample of the decode step.
+class CpuDecodeStep:
+    """The reference's CPU arithmetic for one Efkolos decode step at batch 1.
 
-    Sample: layer 0's four projections plus the LM head at M=1 (one fifth of the
-    layer work plus the whole head), Q4_0 blocks from the oracle packer,
-    dequantise + f32 matmul per call, repeated for about `seconds`."""
-    import numpy as np
-    from oracle.q4_oracle_np import COracle
-    from aria_b200.efkolos import EFKOLOS
-    orc = COracle()
-    threads = threads or os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    projs = [p for p in EFKOLOS.all_projections() if p[0].startswith("blk.0.") or p[0] == "lm_head"]
-    items = []
-    for (name, lay, K, N, s) in projs:
-        w = (rng.standard_normal(K * N, dtype=np.float32) * s).astype(np.float16)
-        blocks = orc.quantize_q4_0_f16(w)
-        x = rng.standard_normal((1, K)).astype(np.float16)
-        items.append((blocks, lay, K, N, x, np.zeros(K * N, np.float32), np.zeros(K, np.float32),
-                      np.zeros((1, N), np.float32)))
-    per_pass = sum(K * N // 32 * 18 + K * 2 + N * 2 for (_, _, K, N, _) in projs)
-    passes, t0 = 0, time.perf_counter()
-    while True:
-        for (blocks, lay, K, N, x, ws, xs, y) in items:
-            orc.baseline_projection(blocks, lay, K, N, x, ws, xs, y, threads)
-        passes += 1
+    All 81 projections with the same data flow as the GPU step (residual
+    stream h, attn_out on the first d_model QKV columns, GELU after ffn_up,
+    residual adds, LM head on the final h); each projection dequantises its
+    Q4_0 blocks to f32 and runs the f32 i-p-j matmul of the reference's
+    cpu_matmul (the oracle's restatement of transformer_cuda.rs:549-575 and
+    :3322-3333), as the reference's CPU step re-reads its weights every step
+    (:1059-1166, :1286-1324).  Weights are the oracle packer's blocks of
+    seeded N(0, sigma) f16 weights."""
+
+    def __init__(self, threads: int):
+        import numpy as np
+        from oracle.q4_oracle_np import COracle
+        from aria_b200.efkolos import EFKOLOS
+        self.np = np
+        self.orc = COracle()
+        self.threads = threads
+        self.cfg = EFKOLOS
+        rng = np.random.default_rng(0)
+        self.items = []
+        for (name, lay, K, N, sg) in EFKOLOS.all_projections():
+            w = (rng.standard_normal(K * N, dtype=np.float32) * sg).astype(np.float16)
+            self.items.append((self.orc.quantize_q4_0_f16(w), lay, K, N))
+        big = max(K * N for (_, _, K, N) in self.items)
+        self.ws = np.zeros(big, np.float32)
+        self.xs = np.zeros(max(K for (_, _, K, _) in self.items), np.float32)
+        self.h0 = rng.standard_normal((1, EFKOLOS.d_model)).astype(np.float16)
+        self.bytes_per_step = sum(K * N // 32 * 18 + K * 2 + N * 2 for (_, _, K, N) in self.items)
+
+    def _proj(self, i, x16):
+        blocks, lay, K, N = self.items[i]
+        y = self.np.zeros((1, N), self.np.float32)
+        self.orc.baseline_projection(blocks, lay, K, N, self.np.ascontiguousarray(x16), self.ws, self.xs, y,
+                                     self.threads)
+        return y
+
+    def step(self):
+        from oracle.q4_oracle_np import gelu_tanh
+        np = self.np
+        d = self.cfg.d_model
+        h = self.h0.astype(np.float32)
+        for li in range(self.cfg.num_layers):
+            qkv = self._proj(4 * li, h.astype(np.float16))
+            h = h + self._proj(4 * li + 1, qkv[:, :d].astype(np.float16))
+            u = gelu_tanh(self._proj(4 * li + 2, h.astype(np.float16)))
+            h = h + self._proj(4 * li + 3, u.astype(np.float16))
+        return self._proj(len(self.items) - 1, h.astype(np.float16))
+
+    def rate(self, steps: int) -> tuple[float, float]:
+        """(GB/s, seconds) over `steps` whole steps."""
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            self.step()
         el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return {"value": per_pass * passes / el / 1e9, "unit": UNIT, "cores": threads,
-            "kind": "port", "seconds": el,
-            "sample": f"{passes} passes of layer-0 QKV/attn_out/ffn_up/ffn_down + LM head at M=1 "
-                      f"(dequantise + f32 i-p-j matmul, {threads} OpenMP threads)"}
+        return self.bytes_per_step * steps / el / 1e9, el
+
+
+def cpu_baseline_record(seconds: float = 12.0) -> dict:
+    """CPU baseline for the JSON line: whole decode steps on all host threads for
+    about `seconds`, and one step on a single thread (the reference's cpu_matmul
+    is serial)."""
+    threads = os.cpu_count() or 1
+    cs = CpuDecodeStep(threads)
+    _, one = cs.rate(1)
+    n = max(1, int(seconds / max(one, 1e-3)))
+    v, el = cs.rate(n)
+    cs1 = CpuDecodeStep(1)
+    cs1.items, cs1.ws, cs1.xs, cs1.h0 = cs.items, cs.ws, cs.xs, cs.h0
+    v1, el1 = cs1.rate(1)
+    return {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "seconds": el,
+            "sample": f"{n} whole decode steps (81 chained projections at M=1, dequantise + f32 i-p-j matmul, "
+                      f"{threads} OpenMP threads)",
+            "single_thread": {"value": v1, "unit": UNIT, "cores": 1, "seconds": el1,
+                              "sample": "1 whole decode step on one thread"},
+            "cpu_model": cpu_model(), "nproc": os.cpu_count()}
 
 
 def cpu_model() -> str:
@@ -165,24 +222,92 @@ def cpu_model() -> str:
 
 
 def run_reference(args, rank: int) -> None:
+    """The reference arm: the reference's CPU arithmetic on our workload (whole
+    Efkolos decode steps at batch 1), all host threads; each step is one whole
+    decode step (tens of ms on a 16-core host)."""
     if rank != 0:
         return
-    # each step is one bounded sample; total stays within a few minutes
-    per_step = max(0.5, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
-    for _ in range(args.warmup):
-        cpu_decode_sample(per_step / 4)
-    vals = [cpu_decode_sample(per_step) for _ in range(args.steps)]
-    v = statistics.median([r["value"] for r in vals])
-    cb = dict(vals[0])
-    cb["value"] = v
-    cb["cpu_model"] = cpu_model()
-    cb["nproc"] = os.cpu_count()
+    threads = os.cpu_count() or 1
+    cs = CpuDecodeStep(threads)
+    for _ in range(min(args.warmup, 3)):
+        cs.step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cs.step()
+        times.append(time.perf_counter() - t0)
+    ms = statistics.median(times) * 1e3
+    v = cs.bytes_per_step / (ms * 1e-3) / 1e9
+    cs1 = CpuDecodeStep(1)
+    cs1.items, cs1.ws, cs1.xs, cs1.h0 = cs.items, cs.ws, cs.xs, cs.h0
+    v1, el1 = cs1.rate(1)
+    cb = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+          "sample": f"{args.steps} whole decode steps (81 chained projections at M=1, dequantise + f32 i-p-j "
+                    f"matmul, {threads} OpenMP threads), median step",
+          "single_thread": {"value": v1, "unit": UNIT, "cores": 1, "seconds": el1,
+                            "sample": "1 whole decode step on one thread"},
+          "cpu_model": cpu_model(), "nproc": os.cpu_count()}
     rec = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "efkolos_decode_b1 (BASELINE configs[1]), CPU sample", "M": 1},
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "efkolos_decode_b1 (BASELINE configs[1]): 20 layers x (QKV, attn_out, ffn_up, "
+                                  "ffn_down) + LM head, M=1, model-order chain", "M": 1,
+                      "alg_bytes_per_step": cs.bytes_per_step},
            "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(rec), flush=True)
+
+
+def case_shape(name: str):
+    from aria_b200.efkolos import EFKOLOS, SCALED
+    cfg = SCALED if name.startswith("scaled_") else EFKOLOS
+    base = name.replace("scaled_", "")
+    for (n, lay, K, N, s) in cfg.projections() + [cfg.lm_head()]:
+        if n.endswith(base) or n == base:
+            return lay, K, N, s
+    raise SystemExit(f"unknown case {name}")
+
+
+def run_case(args) -> None:
+    """One projection kind, `--launches` times through the C ABI (small enough
+    for an ncu capture); with --time, chained over weight copies > 4x L2 in a
+    CUDA graph and timed with CUDA events."""
+    import torch
+    from aria_b200 import q4
+    from aria_b200.efkolos import synth_f16
+    lay, K, N, sigma = case_shape(args.case)
+    shape = (K, N) if lay == q4.LAYOUT_KN else (N, K)
+    w = q4.Q4Weight.from_f16(synth_f16(shape, sigma, 1), lay)
+    x = synth_f16((args.M, K), 1.0, 2)
+    y = torch.empty(args.M, N, dtype=torch.float16, device="cuda")
+    for _ in range(args.launches):
+        q4.matmul(x, w, y, kernel=args.kernel)
+    torch.cuda.synchronize()
+    out = {"case": args.case, "K": K, "N": N, "M": args.M, "kernel": kernel_name(w, args.M, flags_for(args.kernel))}
+    if args.time:
+        l2 = torch.cuda.get_device_properties(0).L2_cache_size
+        ncopy = max(4, -(-4 * l2 // w.nbytes))
+        pool = [q4.Q4Weight(w.buf.clone(), lay, K, N) for _ in range(ncopy)]
+        n = max(32, min(256, ncopy))
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            q4.matmul(x, pool[0], y, kernel=args.kernel, const_weights=True)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for j in range(n):
+                    q4.matmul(x, pool[j % ncopy], y, kernel=args.kernel, const_weights=True)
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(5):
+                g.replay()
+            e1.record(s)
+            torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / (5 * n)
+        out.update({"us_per_launch": us, "GBs": (w.nbytes + args.M * (K + N) * 2) / us / 1e3,
+                    "TFLOPs": 2 * args.M * K * N / us / 1e6})
+    print(json.dumps(out), flush=True)
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -208,8 +333,9 @@ def scaled_section(args, rank, world, local_rank, stream, timed, peaks):
     out["decode_b64_colsplit"] = {
         "ms_per_step": ms, "tokens_per_s": 64 / (ms * 1e-3),
         "weight_GBs_per_rank": wb / (ms * 1e-3) / 1e9, "weight_GBs_total": wb * world / (ms * 1e-3) / 1e9,
-        "allgather_bytes_in_per_rank": prog.gathered_bytes(),
-        "split": "ffn_up, ffn_down, LM head column-split over ranks; QKV, attn_out replicated"}
+        "collective_bytes_per_rank": prog.collective_bytes(), "collectives_per_step": prog.collectives_per_step,
+        "split": "ffn_up column-split and ffn_down split along K (one NCCL all-reduce per layer), LM head "
+                 "column-split + all-gather; QKV, attn_out replicated"}
     del g, prog
     torch.cuda.empty_cache()
     stack = Q4Stack.build(SCALED, seed=rank * 1000 + 77)
@@ -232,15 +358,22 @@ def scaled_section(args, rank, world, local_rank, stream, timed, peaks):
     return out
 
 
-# ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of the decode
-# step's dominant kernel kind (profiles/gemv_stream_ffn_down_M1.md, one cold launch)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each
+# decode-step projection kind as its kernel runs in the step, from one ncu
+# capture of `bench.py --case <kind> --M 1` (cold launch)
 NCU_TRAFFIC = {"ffn_down": 1849344}
 
 
-def kernel_name(w, M: int, workspace_bytes: int = 0) -> str:
+def flags_for(kernel: str) -> int:
+    from aria_b200 import _lib
+    return {"auto": 0, "stream": _lib.FLAG_KERNEL_STREAM, "register": _lib.FLAG_KERNEL_REGISTER,
+            "tensor": _lib.FLAG_KERNEL_TENSOR}[kernel]
+
+
+def kernel_name(w, M: int, flags: int = 0, workspace_bytes: int = 0) -> str:
     """The kernel the library routes this projection to (aria_q4_0_kernel_choice)."""
     from aria_b200._lib import lib
-    k = lib().aria_q4_0_kernel_choice(w.layout, w.K, w.N, M, workspace_bytes, 0)
+    k = lib().aria_q4_0_kernel_choice(w.layout, w.K, w.N, M, workspace_bytes, flags)
     return {1: "gemv_stream_kernel", 2: "decode_mma_kernel", 3: "gemm_tc_kernel"}.get(k, f"status {-k}")
 
 
@@ -360,7 +493,7 @@ def cublas_fp16_section(stream, timed, l2: int, q4_decode_ms: float, q4_prefill_
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
-    from aria_b200.efkolos import EFKOLOS, DecodeProgram, Q4Stack
+    from aria_b200.efkolos import EFKOLOS, DecodeProgram, Q4Stack, synth_f16
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -437,7 +570,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         w0 = stack0.weights[idxs[0]][1]
         ncopy = max(4, -(-4 * l2 // w0.nbytes))
         pool = [Q4Weight(w0.buf.clone(), w0.layout, w0.K, w0.N) for _ in range(ncopy)]
-        x_, y_ = prog.xs[idxs[0]], prog.ys[idxs[0]]
+        x_ = synth_f16((1, w0.K), 1.0, 17 + idxs[0])
+        y_ = torch.empty(1, w0.N, dtype=torch.float16, device=dev)
         n_launch = max(64, min(512, ncopy))
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
@@ -458,7 +592,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     wdom = stack0.weights[kinds[dom][0]][1]
     roof = {"bound": "hbm", "kernel": f"{kernel_name(wdom, 1)} ({dom})", "achieved": per_kind[dom]["gbs"],
             "peak": hbm_peak, "unit": "GB/s", "frac": per_kind[dom]["gbs"] / hbm_peak,
-            "traffic": NCU_TRAFFIC.get(dom), "traffic_source": "profiles/gemv_stream_ffn_down_M1.md (ncu, bytes per launch)",
+            "traffic": NCU_TRAFFIC.get(dom), "traffic_source": "ncu dram bytes per launch of this kind (cold)",
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650",
             "per_kind": per_kind}
     for k in per_kind:
@@ -471,14 +605,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     gemv_large = gemv_config4_b1(stream, timed, l2, hbm_peak)
 
     # ---- end to end through the public API with host buffers
-    x_host = torch.empty_like(prog.x_all, device="cpu").pin_memory()
-    x_host.copy_(prog.x_all)
-    out_host = torch.empty_like(prog.ys[-1], device="cpu").pin_memory()
+    x_host = torch.empty_like(prog.h0, device="cpu").pin_memory()
+    x_host.copy_(prog.h0)
+    out_host = torch.empty_like(prog.logits, device="cpu").pin_memory()
 
     def e2e_step(i):
-        prog.x_all.copy_(x_host, non_blocking=True)
+        prog.h0.copy_(x_host, non_blocking=True)
         graphs[i % reps].replay()
-        out_host.copy_(prog.ys[-1], non_blocking=True)
+        out_host.copy_(prog.logits, non_blocking=True)
 
     e2e_ms = timed(e2e_step, args.steps, args.warmup, "aria_e2e") / args.steps
     e2e_val = bytes_step * world / (e2e_ms * 1e-3) / 1e9
@@ -538,12 +672,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_decode_sample(12.0)
-        # the reference's cpu_matmul is serial: also the single-thread rate
-        one = cpu_decode_sample(6.0, threads=1)
-        cpu["single_thread"] = {"value": one["value"], "unit": one["unit"], "cores": 1, "sample": one["sample"]}
-        cpu["cpu_model"] = cpu_model()
-        cpu["nproc"] = os.cpu_count()
+        cpu = cpu_baseline_record(12.0)
 
     rec = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -564,7 +693,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
            "gemv_config4_b1": gemv_large,
            "cublas_fp16_same_box": cublas,
            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": prog.input_bytes(),
-                   "d2h_bytes_per_step": prog.ys[-1].numel() * 2, "ms_per_step": e2e_ms},
+                   "d2h_bytes_per_step": prog.output_bytes(), "ms_per_step": e2e_ms},
            "gpu_launches": prog.launches * args.steps}
     if rank == 0:
         print(json.dumps(rec), flush=True)
@@ -579,6 +708,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.case:
+        run_case(args)
         return
     if world > 1:
         import datetime

@@ -5,14 +5,17 @@
  * binds its GPU work from Rust through cudarc: kernels by name from a PTX module
  * (src/transformer_cuda.rs:832-890) and cuBLAS through the `gemm()` helper
  * (src/transformer_cuda.rs:615-640).  These functions replace, for Q4_0
- * weights, the five projection GEMMs and the CPU packer; a Rust `extern "C"`
- * block for them is given in INTEGRATION.md.
+ * weights, the five projection GEMMs and the CPU packer.
  *
  * Conventions (all entry points):
  *   - every pointer is a device pointer unless stated otherwise; `stream` is a
  *     cudaStream_t (CUstream) passed as void*, NULL = legacy default stream;
- *   - calls are stream-ordered and asynchronous: no host synchronisation, no
- *     allocation, no global mutable state (safe on distinct streams/threads);
+ *   - calls are stream-ordered and asynchronous: no host synchronisation and
+ *     no allocation.  Calls on distinct streams or threads share no buffers
+ *     except two per-device objects: the device error code of the bounded
+ *     waits (aria_q4_take_device_error: one per device, so a wait that expires
+ *     in one stream is reported to whichever thread reads the code first) and
+ *     the static scratch of aria_q4_0_matmul_static_ws;
  *   - the return value is an aria_q4_status; nothing aborts the process
  *     (the reference unwraps and aborts on any CUDA error, Cargo.toml:24);
  *   - layouts name the orientation of the reference's flat f16 tensor:
@@ -150,13 +153,20 @@ ARIA_Q4_API size_t aria_q4_0_workspace_bytes(int K, int N, int M);
  * tiles than SMs it splits K into work units whose f32 partials go to the
  * workspace; the last unit of each tile adds them in slice order (results are
  * reproducible).  The workspace must be zero-filled before its first use;
- * every call, of any shape, leaves it ready for the next.  Calls that share a
- * workspace must be ordered (one stream, or events). */
+ * every call, of any shape, leaves it ready for the next -- except a call
+ * during which a bounded wait expired (aria_q4_take_device_error() != 0):
+ * zero the workspace's first aria_q4_0_workspace_counter_bytes() bytes
+ * again before reusing it.  Calls that share a workspace must be ordered (one
+ * stream, or events). */
 ARIA_Q4_API int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N,
                         const uint16_t* x, int M, int ldx,
                         void* y, int y_dtype, int ldy,
                         const uint16_t* bias, float alpha, float beta,
                         void* workspace, size_t workspace_bytes, int flags, void* stream);
+
+/* Bytes at the start of every workspace that hold the split-K tile counters
+ * (the region that must be zero before a call). */
+ARIA_Q4_API size_t aria_q4_0_workspace_counter_bytes(void);
 
 /* Kernels aria_q4_0_matmul_ws can run. */
 enum {
@@ -171,13 +181,23 @@ enum {
  * benchmarks and tests). */
 ARIA_Q4_API int aria_q4_0_kernel_choice(int layout, int K, int N, int M, size_t workspace_bytes, int flags);
 
-/* aria_q4_0_matmul_ex that allocates nothing: when the tensor-core kernel would
- * split K it uses the library's own static device scratch (8 MiB per device)
- * instead of a caller workspace, first clearing its counter region on the
- * stream; ARIA_Q4_ESIZE when the split needs more than that.  Every call on a
- * device shares that one scratch: calls that overlap in time (unordered
- * streams, or several host threads) corrupt each other's partial sums, so
- * order them on one stream.  No counterpart in the reference. */
+/* aria_q4_0_matmul_ex for callers that cannot allocate device memory: those
+ * that run inside another framework's memory pool or a captured CUDA graph
+ * where cudaMalloc is not allowed, or that hold no allocator at all (a
+ * foreign-language host calling through this C ABI).  Where the tensor-core
+ * kernel splits K it uses the library's own static device scratch -- a
+ * file-scope 8 MiB array that every GPU which loads the library holds until
+ * the process exits -- in place of a caller workspace, choosing only splits
+ * whose partials fit in it (a shape whose best split would need more runs with
+ * a smaller split or none).  The call allocates nothing.  The first call on a
+ * device looks up the array's device address once (cudaGetSymbolAddress), so
+ * make it before any stream capture; that cached address does not survive
+ * cudaDeviceReset.  Each call that splits K first clears the scratch's
+ * counter region on the stream.  Every call on a device shares that one
+ * scratch and it keeps the last call's contents: calls that overlap on the GPU
+ * (unordered streams, or several host threads) race and corrupt each other's
+ * partial sums, so order them on one stream.  No counterpart in the
+ * reference. */
 ARIA_Q4_API int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K, int N,
                         const uint16_t* x, int M, int ldx,
                         void* y, int y_dtype, int ldy,
@@ -188,12 +208,34 @@ ARIA_Q4_API int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K,
 ARIA_Q4_API const char* aria_q4_strerror(int status);
 /* cudaError_t of the last failing CUDA call on this thread (0 if none). */
 ARIA_Q4_API int aria_q4_last_cuda_error(void);
+/* Device-side error codes (aria_q4_take_device_error). */
+enum {
+  ARIA_Q4_DEVERR_NONE = 0,
+  ARIA_Q4_DEVERR_TIMEOUT_FULL = 1,   /* the MMA issuer waited too long for an operand stage */
+  ARIA_Q4_DEVERR_TIMEOUT_EMPTY = 2,  /* a producer waited too long for a free stage */
+  ARIA_Q4_DEVERR_TIMEOUT_ACCUM = 3   /* an accumulator hand-off waited too long */
+};
+
 /* Reads and clears the device-side error code of the current device: 0 = none,
- * 1..3 = a bounded wait inside the tcgen05 kernel expired (the kernel returned
- * without finishing its tile instead of hanging), -1 = the read failed.
- * Synchronises the device.  No reference counterpart (the reference aborts). */
+ * ARIA_Q4_DEVERR_* = a bounded wait inside the tcgen05 kernel expired (the
+ * kernel recorded the first such wait, unwound and returned without finishing
+ * its tiles instead of hanging), -1 = the read failed.  One code per device,
+ * shared by every stream and thread.  Synchronises the device.  No reference
+ * counterpart (the reference aborts). */
 ARIA_Q4_API int aria_q4_take_device_error(void);
 ARIA_Q4_API int aria_q4_abi_version(void);
+
+/* ---------------------------------------------------------------- test hook */
+
+/* Runs the tcgen05 kernel (no K split) with its activation-tile producer
+ * issuing no copies and every pipeline wait limited to wait_limit_us
+ * (1..1000000): the MMA issuer's first wait then runs out, the kernel records
+ * ARIA_Q4_DEVERR_TIMEOUT_FULL, releases its tensor memory and returns, and y
+ * is left unspecified.  Exists so that tests can drive the failure path
+ * without faulting the GPU; no reference counterpart. */
+ARIA_Q4_API int aria_q4_test_tensor_stall(const void* tiled, int layout, int K, int N,
+                        const uint16_t* x, int M, int ldx,
+                        void* y, int y_dtype, int ldy, unsigned wait_limit_us, void* stream);
 
 #ifdef __cplusplus
 }

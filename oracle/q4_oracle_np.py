@@ -97,6 +97,30 @@ def dequantize_q4_0(blocks, n: int) -> np.ndarray:
     return w.reshape(-1)[:n]
 
 
+def dequantize_columns(blocks, layout: int, K: int, N: int, cols) -> np.ndarray:
+    """Exact (q - 8) * scale of the output columns `cols` of a K x N projection
+    stored as GGUF Q4_0 blocks in the reference's flat order, as f32 [K][len(cols)].
+
+    KN (w[k][n], blocks along n): element (k, n) sits in block (k*N + n) // 32
+    at position (k*N + n) % 32.  NK (embed[n][k], blocks along k): column n is
+    row n of the stored tensor, blocks n*K/32 .. (n+1)*K/32 - 1.  Lets a parity
+    test check a seeded sample of the outputs of a projection too large to
+    dequantise whole."""
+    b = np.asarray(blocks, dtype=np.uint8).reshape(-1, BLOCK_BYTES)
+    cols = np.asarray(cols, dtype=np.int64).reshape(-1)
+    if layout == LAYOUT_NK:
+        nb = K // BLOCK
+        idx = (cols[:, None] * nb + np.arange(nb)[None, :]).reshape(-1)
+        rows = dequantize_q4_0(b[idx].reshape(-1), idx.size * BLOCK).reshape(cols.size, K)
+        return np.ascontiguousarray(rows.T)
+    flat = np.arange(K, dtype=np.int64)[:, None] * N + cols[None, :]
+    blk, pos = flat // BLOCK, flat % BLOCK
+    scale = b[:, 0:2].copy().view(np.float16).astype(np.float32).reshape(-1)[blk]
+    byte = b[blk, 2 + pos // 2].astype(np.int32)
+    q = (byte >> (4 * (pos % 2))) & 0xF
+    return ((q - 8).astype(np.float32) * scale).astype(np.float32)
+
+
 def matmul_ref(blocks, layout: int, K: int, N: int, x_f16, bias_f16=None, alpha: float = 1.0) -> np.ndarray:
     """fp64 parity reference: y[M,N] = alpha * x[M,K] @ W(K,N) (+ bias)."""
     w = dequantize_q4_0(blocks, K * N).astype(np.float64)

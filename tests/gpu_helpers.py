@@ -72,12 +72,31 @@ def check_close(y, ref, max_abs=1e-2, rel_l2=1e-3, what=""):
     return mx, rl2
 
 
+def sampled_ref(blocks, layout, K, N, x_f16, cols, bias_f16=None, alpha=1.0):
+    """fp64 reference of the output columns `cols` only (for projections too
+    large to dequantise whole in a test): alpha * x @ W[:, cols] (+ bias[cols])."""
+    from oracle.q4_oracle_np import dequantize_columns
+    W = dequantize_columns(blocks, layout, K, N, cols).astype(np.float64)
+    y = alpha * (np.asarray(x_f16, dtype=np.float16).astype(np.float64).reshape(-1, K) @ W)
+    if bias_f16 is not None:
+        y = y + np.asarray(bias_f16, dtype=np.float16).astype(np.float64)[cols][None, :]
+    return y
+
+
+def sample_columns(N, n, seed):
+    """A seeded sample of n output columns of N, always holding the first and last."""
+    cols = np.sort(np.random.default_rng(seed).choice(N, min(N, n), replace=False))
+    cols[0], cols[-1] = 0, N - 1
+    return np.unique(cols)
+
+
 def run_projection(q4, coracle, layout, K, N, M, out_dtype=None, bias=False, alpha=1.0, beta=0.0, seed=0,
-                   wscale=0.02, ldx=None, flags=0, gelu=False):
+                   wscale=0.02, ldx=None, flags=0, gelu=False, cols=None):
     """One aria_q4_0_matmul call on seeded inputs, checked for canary damage;
     returns (y, fp64 reference).  ldx > K leaves a gap after each x row.  gelu:
     request the GELU epilogue (ARIA_Q4_FLAG_EPILOGUE_GELU) and apply it to the
-    reference before the beta term."""
+    reference before the beta term.  cols: check only these output columns (the
+    GPU still computes all N; y and the reference are returned for cols)."""
     import torch
     if out_dtype is None:
         out_dtype = torch.float32
@@ -88,7 +107,10 @@ def run_projection(q4, coracle, layout, K, N, M, out_dtype=None, bias=False, alp
     x = rng.standard_normal((M, K)).astype(np.float16)
     b = (rng.standard_normal(N) * 0.1).astype(np.float16) if bias else None
     blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
-    ref = coracle.matmul_ref(blocks, layout, K, N, x, b, alpha)
+    if cols is None:
+        ref = coracle.matmul_ref(blocks, layout, K, N, x, b, alpha)
+    else:
+        ref = sampled_ref(blocks, layout, K, N, x, cols, b, alpha)
     if gelu:
         from oracle.q4_oracle_np import gelu_tanh
         ref = gelu_tanh(ref)
@@ -114,9 +136,11 @@ def run_projection(q4, coracle, layout, K, N, M, out_dtype=None, bias=False, alp
         call("aria_q4_0_matmul", *args, _stream())
     out = yt.cpu().to(torch.float64).numpy()
     y_init = torch.from_numpy(y0).to(out_dtype).to(torch.float64).numpy()
+    sel = slice(None) if cols is None else cols
     if beta != 0.0:
-        ref = ref + beta * y_init[1:M + 1, :N]
+        ref = ref + beta * y_init[1:M + 1, :N][:, sel]
     # canaries
     assert np.array_equal(out[0], y_init[0]) and np.array_equal(out[M + 1], y_init[M + 1]), "row canary"
     assert np.array_equal(out[1:M + 1, N:], y_init[1:M + 1, N:]), "column canary"
-    return out[1:M + 1, :N], ref
+    assert np.isfinite(out[1:M + 1, :N]).all()
+    return out[1:M + 1, :N][:, sel], ref

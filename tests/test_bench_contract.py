@@ -27,8 +27,16 @@ def test_reference_arm_json_line():
     assert cb["sample"] and cb["cpu_model"] and cb["nproc"] >= 1
 
 
-def test_cpu_sampler_single_thread():
+def test_cpu_decode_step_chains_like_the_gpu_step():
+    """The CPU step (reference arithmetic) runs the 81 projections in order, one
+    thread, and its bytes per step are the GPU step's algorithmic bytes."""
     sys.path.insert(0, ROOT)
     import bench
-    r = bench.cpu_decode_sample(0.3, threads=1)
-    assert r["cores"] == 1 and r["value"] > 0 and r["unit"] == "GB/s" and r["kind"] == "port"
+    from aria_b200.efkolos import EFKOLOS
+    cs = bench.CpuDecodeStep(threads=1)
+    assert len(cs.items) == 4 * EFKOLOS.num_layers + 1
+    assert cs.bytes_per_step == sum(K * N // 32 * 18 + 2 * (K + N) for (_, _, K, N, _) in EFKOLOS.all_projections())
+    logits = cs.step()
+    assert logits.shape == (1, EFKOLOS.vocab_size)
+    import numpy as np
+    assert np.isfinite(logits).all()

@@ -93,3 +93,34 @@ def test_kernel_choice_routing():
         assert L.aria_q4_0_kernel_choice(KN, 896, 3584, M, 0, 16) == L.aria_q4_0_kernel_choice(KN, 896, 3584, M, 0, 0)
     assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 32) == -1          # unknown flag
 
+
+
+def test_static_scratch_validation_needs_no_gpu(lib):
+    """aria_q4_0_matmul_static_ws validates its arguments before touching the
+    device, and no longer rejects shapes by the unlimited plan's scratch size:
+    a forced register-kernel call at M = 64 on a tall K (whose tensor-core plan
+    would want more than the 8 MiB scratch) and a plan that only fits with a
+    smaller split both get past validation to the device check (which fails on
+    a host without a GPU with ECUDA or ENODEVICE, never ESIZE)."""
+    P = ctypes.c_void_p
+    args = lambda K, N, M: (P(256), 0, K, N, P(256), M, K, P(256), 0, N, None, 1.0, 0.0)  # noqa: E731
+    assert lib.aria_q4_0_matmul_static_ws(*args(64, 64, 1), 64, None) == 1         # unknown flag
+    assert lib.aria_q4_0_matmul_static_ws(*args(64, 64, 1), 2 | 4, None) == 1      # two kernels
+    assert lib.aria_q4_0_matmul_static_ws(*args(64, 48, 1), 0, None) == 2          # KN needs N % 32 == 0
+    assert lib.aria_q4_0_matmul_static_ws(*args(64, 64, 0), 0, None) == 0          # M == 0: nothing to do
+    assert lib.aria_q4_0_matmul_static_ws(*args(64, 64, 9), 2, None) == 2          # stream takes M <= 8
+    assert lib.aria_q4_0_workspace_bytes(16384, 4096, 64) > 0
+    for flags in (4, 0):
+        rc = lib.aria_q4_0_matmul_static_ws(*args(16384, 4096, 64), flags, None)
+        assert rc in (4, 5), rc
+    assert lib.aria_q4_0_workspace_bytes(16384, 4096, 128) > 8 << 20
+    assert lib.aria_q4_0_kernel_choice(0, 16384, 4096, 128, 8 << 20, 0) == 3
+    assert lib.aria_q4_0_matmul_static_ws(*args(16384, 4096, 128), 0, None) in (4, 5)
+    assert lib.aria_q4_0_workspace_counter_bytes() > 0
+
+
+def test_stall_hook_validates_without_gpu(lib):
+    P = ctypes.c_void_p
+    assert lib.aria_q4_test_tensor_stall(P(256), 0, 64, 64, P(256), 1, 64, P(256), 0, 64, 0, None) == 1
+    assert lib.aria_q4_test_tensor_stall(P(256), 0, 64, 48, P(256), 1, 64, P(256), 0, 64, 100, None) == 2
+    assert lib.aria_q4_test_tensor_stall(P(256), 0, 64, 64, P(256), 1, 64, P(256), 0, 64, 100, None) in (4, 5)

@@ -98,3 +98,60 @@ def test_ranges_cover_exactly():
         for world in (1, 2, 3, 8):
             rs = [adist.batch_range(N, world, r) for r in range(world)]
             assert sum(b - a for a, b in rs) == N and rs[0][0] == 0 and rs[-1][1] == N
+
+
+def _pair_worker(rank, world, port, d, ff, M, q):
+    """ffn_up column slice -> ffn_down K slice -> all-reduce, oracle arithmetic."""
+    import torch.distributed as dist
+    from oracle import q4_oracle_np as npo
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(1)
+        up = torch.from_numpy((rng.standard_normal((d, ff)) * 0.02).astype(np.float16))
+        dn = torch.from_numpy((rng.standard_normal((ff, d)) * 0.02).astype(np.float16))
+        h = rng.standard_normal((M, d)).astype(np.float16)
+        us = adist.ColumnSplit(0, d, ff, world, rank, align_to=128)
+        ds = adist.RowSplit(0, ff, d, world, rank, align=128)
+        same = us.cols == ds.rows
+        k0, k1 = ds.rows
+        part = np.zeros((M, d))
+        if k1 > k0:
+            u = npo.gelu_tanh(npo.matmul_ref(npo.quantize_q4_0_f16(us.slice_weight(up).numpy().reshape(-1)), 0, d,
+                                             k1 - k0, h)).astype(np.float16)
+            part = npo.matmul_ref(npo.quantize_q4_0_f16(ds.slice_weight(dn).numpy().reshape(-1)), 0, k1 - k0, d, u)
+        t = torch.from_numpy(part)
+        dist.all_reduce(t)
+        u_full = npo.gelu_tanh(npo.matmul_ref(npo.quantize_q4_0_f16(up.numpy().reshape(-1)), 0, d, ff, h))
+        ref = npo.matmul_ref(npo.quantize_q4_0_f16(dn.numpy().reshape(-1)), 0, ff, d, u_full.astype(np.float16))
+        q.put((rank, same, float(np.abs(t.numpy() - ref).max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,d,ff,M", [(2, 64, 512, 3), (3, 96, 640, 2)])
+def test_ffn_pair_split_allreduce_gloo(world, d, ff, M):
+    """ffn_up split by columns and ffn_down split along K on the same ranges:
+    the all-reduced partial products equal the unsplit pair (the Q4_0 blocks of
+    K-slices of a KN tensor are the full tensor's blocks, so only the f32
+    summation order differs)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pair_worker, args=(r, world, port, d, ff, M, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    import queue as _queue
+    res = []
+    while len(res) < world:
+        try:
+            res.append(q.get(timeout=2))
+        except _queue.Empty:
+            assert not [p for p in procs if p.exitcode not in (None, 0)], "a rank failed"
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, same, err in res:
+        assert same, f"rank {rank}: ffn_up columns and ffn_down rows differ"
+        assert err < 1e-9, f"rank {rank}: all-reduced pair off by {err}"

@@ -163,3 +163,37 @@ def test_one_workspace_serves_any_shape_sequence(q4, coracle):
 def test_no_device_error_recorded(q4):
     from aria_b200 import _lib
     assert _lib.lib().aria_q4_take_device_error() == 0
+
+
+CONFIG4 = [("ffn_up", LAYOUT_KN, 4096, 16384), ("ffn_down", LAYOUT_KN, 16384, 4096),
+           ("lm_head", LAYOUT_NK, 4096, 31500)]
+
+
+@pytest.mark.parametrize("name,layout,K,N", CONFIG4)
+@pytest.mark.parametrize("M", [64, 4096])
+def test_config4_full_shape_sampled(q4, coracle, name, layout, K, N, M):
+    """BASELINE config 4 projections at their full shapes: M = 4096 (prefill,
+    tcgen05 kernel) and M = 64 (batched decode through the auto workspace, so
+    K is split where the planner splits it).  The weight is uploaded as GGUF
+    blocks (repack at full size).  The GPU computes every output; a seeded
+    sample of rows x columns (first and last of each included) is checked
+    against the fp64 oracle."""
+    from aria_b200 import _lib
+    from tests.gpu_helpers import sample_columns, sampled_ref
+    rng = np.random.default_rng(K + N + M)
+    shape = (K, N) if layout == LAYOUT_KN else (N, K)
+    w = (rng.standard_normal(shape, dtype=np.float32) * 0.02).astype(np.float16)
+    blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
+    del w
+    x = rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+    wq = q4.Q4Weight.from_gguf_blocks(torch.from_numpy(blocks).cuda(), layout, K, N)
+    if M == 64:
+        ws = int(_lib.lib().aria_q4_0_workspace_bytes(K, N, M))
+        assert _lib.lib().aria_q4_0_kernel_choice(layout, K, N, M, ws, 0) == 3  # tcgen05
+    y = q4.matmul(torch.from_numpy(x).cuda(), wq)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([[0, M - 1], np.random.default_rng(M).choice(M, min(M, 48), replace=False)]))
+    cols = sample_columns(N, 512, seed=N)
+    got = y[torch.from_numpy(rows).cuda()][:, torch.from_numpy(cols).cuda()].cpu().to(torch.float64).numpy()
+    check_close(got, sampled_ref(blocks, layout, K, N, x[rows], cols), what=f"config4 {name} M={M}")
+    assert bool(torch.isfinite(y).all())

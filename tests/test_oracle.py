@@ -109,3 +109,19 @@ def test_gelu_tanh_restatement():
     grid = np.linspace(-4, 4, 801)
     exact = np.array([0.5 * v * (1.0 + math.erf(v / math.sqrt(2.0))) for v in grid])
     assert np.max(np.abs(gelu_tanh(grid) - exact)) < 1e-3
+
+
+@pytest.mark.parametrize("layout,K,N", [(npo.LAYOUT_KN, 96, 64), (npo.LAYOUT_KN, 256, 352),
+                                        (npo.LAYOUT_NK, 128, 37), (npo.LAYOUT_NK, 64, 300)])
+def test_dequantize_columns_matches_full_dequantisation(coracle, layout, K, N):
+    """The column-sampling dequantiser used by the sampled parity tests equals
+    slicing the full dequantisation, in both orientations."""
+    rng = np.random.default_rng(K + N)
+    shape = (K, N) if layout == npo.LAYOUT_KN else (N, K)
+    w = (rng.standard_normal(shape) * 0.05).astype(np.float16)
+    blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
+    full = npo.dequantize_q4_0(blocks, K * N).reshape(shape)
+    W = full if layout == npo.LAYOUT_KN else full.T
+    cols = rng.choice(N, min(N, 29), replace=False)
+    cols[0] = N - 1
+    assert np.array_equal(npo.dequantize_columns(blocks, layout, K, N, cols), W[:, cols])
