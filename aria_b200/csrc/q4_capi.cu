@@ -22,7 +22,7 @@ cudaError_t launch_gemv(const uint8_t* tiled, int layout, int K, int N, const __
                         bool const_weights);
 cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                            int ydt, int ldy, const __half* bias, float alpha, float beta, void* workspace,
-                           size_t workspace_bytes, cudaStream_t st, bool pdl,
+                           size_t workspace_bytes, cudaStream_t st, bool pdl, bool const_weights,
                            unsigned long long wait_ns = 1000000000ull, bool no_x_loads = false);
 size_t tc_workspace_bytes(int K, int N, int M);
 size_t tc_workspace_used(int K, int N, int M, size_t ws_avail);
@@ -199,7 +199,7 @@ int aria_q4_0_matmul_ws(const void* tiled, int layout, int K, int N, const uint1
     return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, out, ldy,
                                      (const __half*)bias, alpha, beta, st, true, cw));
   return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, out, ldy,
-                                    (const __half*)bias, alpha, beta, workspace, workspace_bytes, st, true));
+                                    (const __half*)bias, alpha, beta, workspace, workspace_bytes, st, true, cw));
 }
 
 size_t aria_q4_0_workspace_counter_bytes(void) { return tc_workspace_counter_bytes(); }
@@ -286,7 +286,7 @@ int aria_q4_test_tensor_stall(const void* tiled, int layout, int K, int N, const
   if (wait_limit_us == 0 || wait_limit_us > 1000000u) return ARIA_Q4_EINVAL;
   if (int s = check_device()) return s;
   return cuda_status(launch_gemm_tc((const uint8_t*)tiled, layout, K, N, (const __half*)x, M, ldx, y, y_dtype, ldy,
-                                    nullptr, 1.0f, 0.0f, nullptr, 0, (cudaStream_t)stream, false,
+                                    nullptr, 1.0f, 0.0f, nullptr, 0, (cudaStream_t)stream, false, false,
                                     (unsigned long long)wait_limit_us * 1000ull, true));
 }
 

@@ -235,31 +235,58 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) 
 constexpr int kOutF16 = 1;
 constexpr int kOutGelu = 2;
 
-// GELU, tanh form, in f32 as the reference's gelu_fwd computes it
-// (lold3344/ARIA src/kernels.cu:574-583): 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
-// (Hendrycks & Gimpel's approximation; tanhf is CUDA's).  Kept out of line: the
-// tensor-core epilogue tests the flag per element, and an inlined tanhf in the
-// not-taken branch bloated its unrolled store and split-K reduction loops
-// (measured: 9% slower batched decode with the flag off).
-static __device__ __noinline__ float gelu_tanh(float v) {
-  const float c = 0.7978845608f;  // sqrt(2 / pi)
-  return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
+// GELU, tanh form, as the reference's gelu_fwd states it (lold3344/ARIA
+// src/kernels.cu:574-583): 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
+// (Hendrycks & Gimpel's approximation).  Evaluated through the identity
+// 0.5 (1 + tanh u) = 1 / (1 + exp(-2u)), i.e. v / (1 + exp(-2u)), with the
+// hardware exp and divide intrinsics: relative error ~1e-6, far below the one
+// f16 rounding of the output, in ~8 instructions inline (an out-of-line
+// accurate tanhf made the fused epilogue of a prefill projection 3-4x slower).
+// Large negative v: exp -> +inf and the quotient -> 0, as GELU does.
+__device__ __forceinline__ float gelu_fast(float v) {
+  const float m2u = -1.5957691216f * fmaf(0.044715f * v, v * v, v);  // -2 sqrt(2/pi) (v + 0.044715 v^3)
+  return __fdividef(v, 1.0f + __expf(m2u));
 }
 
-// One output value: [GELU](v) + beta * y, f16 or f32.  The activation is a
-// template argument: callers branch on (ydt & kOutGelu) once, outside their
-// store loops, so the loop without it holds no call.
-template <bool GELU>
-__device__ __forceinline__ void store_out(void* y, int ydt, size_t idx, float v, float beta) {
-  if (GELU) v = gelu_tanh(v);
-  if ((ydt & kOutF16) == 0) {
-    float* yp = reinterpret_cast<float*>(y) + idx;
-    if (beta != 0.0f) v += beta * *yp;
-    *yp = v;
+// Epilogue of CAP outputs of one thread: y[idx(i)] = [GELU](v[i]) + beta *
+// y[idx(i)] for the i with ok(i), f16 or f32 (ydt).  idx and ok are functors
+// of i; idx(i) must be a valid output index for EVERY i (masked elements point
+// at some in-range output, e.g. clamped coordinates).  The old values are then
+// loaded unconditionally, all before the first store: a load of y cannot move
+// above a store to y (they may alias) and a predicated load feeding a select
+// stalls on its result, so a guarded read-modify-write per element serialises
+// one memory round trip per output (measured 6x slower on B200; the residual
+// add had made a prefill projection up to 9x slower that way).
+template <int CAP, class Idx, class Ok>
+__device__ __forceinline__ void store_outputs(void* y, int ydt, float (&v)[CAP], float beta, Idx idx, Ok ok) {
+  if (ydt & kOutGelu) {
+#pragma unroll
+    for (int i = 0; i < CAP; i++) v[i] = gelu_fast(v[i]);
+  }
+  if (ydt & kOutF16) {
+    __half* yp = reinterpret_cast<__half*>(y);
+    if (beta != 0.0f) {
+      __half old[CAP];
+#pragma unroll
+      for (int i = 0; i < CAP; i++) old[i] = yp[idx(i)];
+#pragma unroll
+      for (int i = 0; i < CAP; i++) v[i] = fmaf(beta, __half2float(old[i]), v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < CAP; i++)
+      if (ok(i)) yp[idx(i)] = __float2half_rn(v[i]);
   } else {
-    __half* yp = reinterpret_cast<__half*>(y) + idx;
-    if (beta != 0.0f) v += beta * __half2float(*yp);
-    *yp = __float2half_rn(v);
+    float* yp = reinterpret_cast<float*>(y);
+    if (beta != 0.0f) {
+      float old[CAP];
+#pragma unroll
+      for (int i = 0; i < CAP; i++) old[i] = yp[idx(i)];
+#pragma unroll
+      for (int i = 0; i < CAP; i++) v[i] = fmaf(beta, old[i], v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < CAP; i++)
+      if (ok(i)) yp[idx(i)] = v[i];
   }
 }
 

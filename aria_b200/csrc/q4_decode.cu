@@ -34,8 +34,6 @@
 // L2 -- or, when the caller declares the weights constant (not written by the
 // preceding kernel), loads its first batch of codes and scales into registers
 // -- so weight streaming overlaps the previous kernel's tail.
-#include <type_traits>
-
 #include "q4_common.cuh"
 
 namespace aria_q4 {
@@ -261,27 +259,18 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
     if (oka) bia = __half2float(a.bias[ra]);
     if (okb) bib = __half2float(a.bias[rb]);
   }
-  // the GELU decision is taken once, so the loop without it holds no call
-  auto store_all = [&](auto gelu) {
-    constexpr bool kGelu = decltype(gelu)::value;
+  float o[NT * 4];
 #pragma unroll
-    for (int j = 0; j < NT; j++) {
+  for (int j = 0; j < NT; j++)
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const int tok = m0 + 8 * j + 2 * t + (e & 1);
-        const bool rowb = e >= 2;
-        const int n = rowb ? rb : ra;
-        if (tok < a.M && (rowb ? okb : oka)) {
-          const float v = a.alpha * acc[j][e] + (rowb ? bib : bia);
-          store_out<kGelu>(a.y, a.ydt, (size_t)tok * a.ldy + n, v, a.beta);
-        }
-      }
-    }
-  };
-  if (a.ydt & kOutGelu)
-    store_all(std::true_type{});
-  else
-    store_all(std::false_type{});
+    for (int e = 0; e < 4; e++) o[4 * j + e] = a.alpha * acc[j][e] + (e >= 2 ? bib : bia);
+  // element i = 4j + e: row ra (rb for e >= 2), token m0 + 8j + 2t + (e & 1)
+  auto tok = [&](int i) { return m0 + 8 * (i >> 2) + 2 * t + (i & 1); };
+  auto row = [&](int i) { return (i & 3) >= 2 ? rb : ra; };
+  store_outputs<NT * 4>(
+      a.y, a.ydt, o, a.beta,
+      [&](int i) { return (size_t)min(tok(i), a.M - 1) * a.ldy + min(row(i), a.N - 1); },
+      [&](int i) { return tok(i) < a.M && ((i & 3) >= 2 ? okb : oka); });
 }
 
 template <int LAYOUT, int NT, int MAXB, bool PRE>

@@ -63,6 +63,9 @@ struct TcArgs {
   // failure-path test only: the X-tile producer issues no copies, so the MMA
   // issuer's first wait runs out and the CTA unwinds
   int no_x_loads;
+  // the weights are not written by the preceding kernel on the stream: the
+  // dequantisers may load and dequantise them before that kernel completes
+  int const_weights;
 };
 
 // K-slice of work unit `unit` in 128-k groups: [g0, g1)
@@ -192,7 +195,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   grid_dep_launch();
-  grid_dep_wait();
+  // Programmatic dependent launch: the X tiles, the outputs (and, with split-K,
+  // the workspace) may be written or read by the preceding kernel, so the X
+  // producer, the MMA issuer and the epilogue wait for it to complete.  The
+  // weights are constants when the caller says so: the dequantisers then fill
+  // the first A stages of tensor memory while that kernel drains (their waits
+  // for free stages, bounded at twice the limit, then include its tail).
+  if (!a.const_weights || warp >= 8) grid_dep_wait();
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
@@ -445,20 +454,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int rr = q * 32 + lane;
     const int KG = a.Kp >> 7;
-    // one output value: [gelu](alpha * acc + bias) (+ beta * y), f16 or f32
-    auto store = [&](int tok, int n, float acc, float bias) {
-      float o = fmaf(a.alpha, acc, bias);
-      if (a.ydt & kOutGelu) o = gelu_tanh(o);
-      const size_t idx = (size_t)tok * a.ldy + n;
-      if ((a.ydt & kOutF16) == 0) {
-        float* yp = reinterpret_cast<float*>(a.y) + idx;
-        if (a.beta != 0.0f) o += a.beta * *yp;
-        *yp = o;
-      } else {
-        __half* yp = reinterpret_cast<__half*>(a.y) + idx;
-        if (a.beta != 0.0f) o += a.beta * __half2float(*yp);
-        *yp = __float2half_rn(o);
-      }
+    // 32 outputs of one row n, tokens tok0 .. tok0 + ntok - 1 (stride ldy), through
+    // store_outputs: the activation, every old value for the beta term loaded
+    // (unconditionally: masked tokens read the last valid one) before the first
+    // store, then the stores
+    auto store32 = [&](int tok0, int ntok, int n, float (&o)[32]) {
+      store_outputs<32>(
+          a.y, a.ydt, o, a.beta, [&](int jj) { return (size_t)(tok0 + min(jj, ntok - 1)) * a.ldy + n; },
+          [&](int jj) { return jj < ntok; });
     };
     for (int j = 0; j < my_tiles; j++) {
       const int buf = NACC == 2 ? (j & 1) : 0;
@@ -491,24 +494,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int tok0 = m0 + cc * 32;
           if (!row_ok || tok0 >= a.M) continue;
           const int ntok = min(32, a.M - tok0);
-          if (a.ydt == kOutF16 && a.beta == 0.0f) {  // f16 out, no activation or accumulate: the common path
-            __half* yp = reinterpret_cast<__half*>(a.y) + (size_t)tok0 * a.ldy + n;
-            if (ntok == 32) {
+          float o[32];
 #pragma unroll
-              for (int jj = 0; jj < 32; jj++)
-                yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
-            } else {
-#pragma unroll
-              for (int jj = 0; jj < 32; jj++)
-                if (jj < ntok) yp[(size_t)jj * a.ldy] = __float2half_rn(fmaf(a.alpha, __uint_as_float(v[jj]), bias));
-            }
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 32; jj++) {
-              if (jj >= ntok) break;
-              store(tok0 + jj, n, __uint_as_float(v[jj]), bias);
-            }
-          }
+          for (int jj = 0; jj < 32; jj++) o[jj] = fmaf(a.alpha, __uint_as_float(v[jj]), bias);
+          store32(tok0, ntok, n, o);
         }
         tc::tc_fence_before();
         __syncwarp();
@@ -538,23 +527,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           __threadfence();
           const float* p0 = a.ws_part + (size_t)tile * a.splits * (128 * BT) + rr;
           if (row_ok) {
-            // eight tokens at a time, every slice's partials loaded before the
-            // first add (up to 64 independent L2 loads in flight per lane)
-            for (int t0 = 0; t0 < BT && m0 + t0 < a.M; t0 += 8) {
-              float v[8][8];
+            // 32 tokens at a time: every slice's partials of 8 tokens loaded before
+            // the first add (up to 64 independent L2 loads in flight per lane)
+            for (int t0 = 0; t0 < BT && m0 + t0 < a.M; t0 += 32) {
+              float o[32];
 #pragma unroll
-              for (int sp = 0; sp < 8; sp++)
-#pragma unroll
-                for (int u = 0; u < 8; u++)
-                  v[sp][u] = sp < a.splits ? __ldcg(p0 + (size_t)sp * (128 * BT) + (size_t)(t0 + u) * 128) : 0.0f;
-#pragma unroll
-              for (int u = 0; u < 8; u++) {
-                float acc = 0.0f;
+              for (int h = 0; h < 4; h++) {
+                float v[8][8];
 #pragma unroll
                 for (int sp = 0; sp < 8; sp++)
-                  if (sp < a.splits) acc += v[sp][u];
-                if (m0 + t0 + u < a.M) store(m0 + t0 + u, n, acc, bias);
+#pragma unroll
+                  for (int u = 0; u < 8; u++)
+                    v[sp][u] = sp < a.splits ? __ldcg(p0 + (size_t)sp * (128 * BT) + (size_t)(t0 + 8 * h + u) * 128)
+                                             : 0.0f;
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                  float acc = 0.0f;
+#pragma unroll
+                  for (int sp = 0; sp < 8; sp++)
+                    if (sp < a.splits) acc += v[sp][u];
+                  o[8 * h + u] = fmaf(a.alpha, acc, bias);
+                }
               }
+              store32(m0 + t0, min(32, a.M - (m0 + t0)), n, o);
             }
           }
           __syncwarp();
@@ -740,11 +735,12 @@ size_t tc_workspace_counter_bytes() { return kTcCounterBytes; }
 // limit and no X copies; every other caller the defaults).
 cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                            int ydt, int ldy, const __half* bias, float alpha, float beta, void* workspace,
-                           size_t workspace_bytes, cudaStream_t st, bool pdl, unsigned long long wait_ns,
-                           bool no_x_loads) {
+                           size_t workspace_bytes, cudaStream_t st, bool pdl, bool const_weights,
+                           unsigned long long wait_ns, bool no_x_loads) {
   TcArgs a;
   a.wait_ns = wait_ns;
   a.no_x_loads = no_x_loads ? 1 : 0;
+  a.const_weights = const_weights ? 1 : 0;
   a.qs = tiled;
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
   a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;

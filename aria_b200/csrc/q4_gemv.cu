@@ -124,28 +124,23 @@ __device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t a0, co
 }
 
 // D fragment element e of a 16-row sub-tile: row g (+8 for e >= 2), token 2t + (e & 1)
-template <int R, bool GELU>
-__device__ __forceinline__ void gemv_store_tile_t(const GemvArgs& a, const float (&v)[R][4], const float (&bias)[R][2],
-                                                  int r0, int g, int t) {
-#pragma unroll
-  for (int r = 0; r < R; r++)
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int n = r0 + 16 * r + g + (e >= 2 ? 8 : 0);
-      const int tok = 2 * t + (e & 1);
-      if (tok < a.M && n < a.N)
-        store_out<GELU>(a.y, a.ydt, (size_t)tok * a.ldy + n, a.alpha * v[r][e] + bias[r][e >> 1], a.beta);
-    }
-}
-
 template <int R>
 __device__ __forceinline__ void gemv_store_tile(const GemvArgs& a, const float (&v)[R][4], const float (&bias)[R][2],
                                                 int r0, int g, int t) {
-  if (a.ydt & kOutGelu)
-    gemv_store_tile_t<R, true>(a, v, bias, r0, g, t);
-  else
-    gemv_store_tile_t<R, false>(a, v, bias, r0, g, t);
+  float o[4 * R];
+#pragma unroll
+  for (int r = 0; r < R; r++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[4 * r + e] = a.alpha * v[r][e] + bias[r][e >> 1];
+  // element i = 4r + e: row r0 + 16r + g (+8 for e >= 2), token 2t + (e & 1)
+  auto row = [&](int i) { return r0 + 16 * (i >> 2) + g + ((i & 3) >= 2 ? 8 : 0); };
+  auto tok = [&](int i) { return 2 * t + (i & 1); };
+  store_outputs<4 * R>(
+      a.y, a.ydt, o, a.beta,
+      [&](int i) { return (size_t)min(tok(i), a.M - 1) * a.ldy + min(row(i), a.N - 1); },
+      [&](int i) { return tok(i) < a.M && row(i) < a.N; });
 }
+
 
 template <int R>
 __device__ __forceinline__ void gemv_load_bias(const GemvArgs& a, float (&b)[R][2], int r0, int g) {
