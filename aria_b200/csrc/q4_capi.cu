@@ -28,6 +28,13 @@ size_t tc_workspace_bytes(int K, int N, int M);
 size_t tc_workspace_used(int K, int N, int M, size_t ws_avail);
 size_t tc_workspace_counter_bytes();
 int take_device_error();
+cudaError_t launch_embed(const __half* embed, const __half* pos_embed, const int* tok, const int* pos, int M, int vocab,
+                         int max_seq, int d, float* h, cudaStream_t st);
+cudaError_t launch_layernorm(const float* x, const __half* g, const __half* b, int M, int d, float eps, __half* y,
+                             int ldy, cudaStream_t st);
+size_t attention_smem_bytes(int dh, int max_seq);
+cudaError_t launch_attention(const __half* qkv, int M, int d, int heads, int max_seq, const int* pos, __half* kc,
+                             __half* vc, __half* out, cudaStream_t st);
 }  // namespace aria_q4
 
 // M at or below which the register-fed decode kernel is used; above it the
@@ -276,6 +283,41 @@ int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K, int N, cons
   if (e != cudaSuccess) return cuda_status(e);
   return aria_q4_0_matmul_ws(tiled, layout, K, N, x, M, ldx, y, y_dtype, ldy, bias, alpha, beta, ws, kStaticWsBytes,
                              flags, stream);
+}
+
+// ------------------------------------------------------------------ decode-step helpers
+int aria_embed_f16(const uint16_t* embed, const uint16_t* pos_embed, int vocab, int max_seq, int d,
+                   const int* tokens, const int* positions, int M, float* h, void* stream) {
+  if (M < 0 || d <= 0 || vocab <= 0 || max_seq <= 0) return ARIA_Q4_EINVAL;
+  if (M == 0) return ARIA_Q4_OK;
+  if (!embed || !pos_embed || !tokens || !positions || !h) return ARIA_Q4_EINVAL;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_embed((const __half*)embed, (const __half*)pos_embed, tokens, positions, M, vocab, max_seq,
+                                  d, h, (cudaStream_t)stream));
+}
+
+int aria_layernorm_f32(const float* x, int M, int d, const uint16_t* gamma, const uint16_t* beta, float eps,
+                       uint16_t* y, int ldy, void* stream) {
+  if (M < 0 || d <= 0 || d > 32 * 256 || ldy < d || !(eps >= 0.0f)) return ARIA_Q4_EINVAL;
+  if (M == 0) return ARIA_Q4_OK;
+  if (!x || !gamma || !beta || !y) return ARIA_Q4_EINVAL;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_layernorm(x, (const __half*)gamma, (const __half*)beta, M, d, eps, (__half*)y, ldy,
+                                      (cudaStream_t)stream));
+}
+
+int aria_attention_decode(const uint16_t* qkv, int M, int d, int heads, uint16_t* k_cache, uint16_t* v_cache,
+                          int max_seq, const int* positions, uint16_t* out, void* stream) {
+  if (M < 0 || d <= 0 || heads <= 0 || d % heads != 0 || max_seq <= 0) return ARIA_Q4_EINVAL;
+  const int dh = d / heads;
+  if (dh % 8 != 0 || 256 % dh != 0) return ARIA_Q4_EUNSUPPORTED;
+  if (attention_smem_bytes(dh, max_seq) > 227 * 1024) return ARIA_Q4_EUNSUPPORTED;
+  if (M == 0) return ARIA_Q4_OK;
+  if (!qkv || !k_cache || !v_cache || !positions || !out) return ARIA_Q4_EINVAL;
+  if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache)) return ARIA_Q4_EALIGN;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_attention((const __half*)qkv, M, d, heads, max_seq, positions, (__half*)k_cache,
+                                      (__half*)v_cache, (__half*)out, (cudaStream_t)stream));
 }
 
 // ------------------------------------------------------------------ failure-path test hook

@@ -1,0 +1,202 @@
+// q4_layer.cu -- the non-projection work of one decode step on the GPU.
+//
+// ARIA decodes with KV cache only on the CPU (lold3344/ARIA
+// src/transformer_cuda.rs `step` :1286-1324 over `cpu_layer_forward`
+// :1059-1166); its GPU forward recomputes the whole prompt every token.  With
+// the Q4_0 projections on the GPU, the rest of a decode step is three small
+// kernels, all stream-ordered and allocation-free:
+//
+//  * embed_kernel      h[m] = embed[token_m] + pos_embed[pos_m]        (:1294-1297)
+//  * layernorm_kernel  y[m] = (x[m] - mean) * rstd * g + b, eps 1e-5    (cpu_layernorm :3271-3293)
+//  * attention_kernel  one new token per sequence: append its k, v to the
+//                      cache at pos_m, then per head softmax(q.K^T / sqrt(dh))
+//                      over positions 0..pos_m and the weighted sum of V
+//                      (:1098-1137; causal: the new token sees itself and
+//                      the cache)
+//
+// The residual stream h stays f32 (the projections add into it through their
+// beta = 1 epilogue); LayerNorm, attention and the KV cache store f16, the
+// activation type the projections read.  One CTA per sequence row (LayerNorm)
+// or per (sequence, head) (attention): these kernels touch kilobytes per token
+// and are latency-bound, not bandwidth-bound.
+#include "q4_common.cuh"
+
+namespace aria_q4 {
+
+constexpr int kLayerThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // red may still be read by a previous call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.0f;
+  for (int w = 0; w < nw; w++) s += red[w];
+  return s;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = -INFINITY;
+  for (int w = 0; w < nw; w++) s = fmaxf(s, red[w]);
+  return s;
+}
+
+// h[m][j] = embed[tok[m]][j] + pos_embed[pos[m]][j] (f16 tables, f32 out);
+// token and position clamped into the tables as the reference clamps them
+// (`tok.min(vocab_size - 1)`, `pos.min(max_seq_len - 1)`, :1291-1292)
+__global__ void __launch_bounds__(kLayerThreads) embed_kernel(const __half* embed, const __half* pos_embed,
+                                                              const int* tok, const int* pos, int vocab, int max_seq,
+                                                              int d, float* h) {
+  const int m = blockIdx.x;
+  const int tk = min(max(tok[m], 0), vocab - 1), ps = min(max(pos[m], 0), max_seq - 1);
+  const __half* e = embed + (size_t)tk * d;
+  const __half* p = pos_embed + (size_t)ps * d;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) h[(size_t)m * d + j] = __half2float(e[j]) + __half2float(p[j]);
+}
+
+// y[m] = (x[m] - mean) * rstd * g + b over d f32 values, f16 out.  Two passes
+// over the row held in registers (mean, then the centred variance), like the
+// reference's f32 LayerNorm.
+template <int PER>  // values per thread: d <= PER * kLayerThreads
+__global__ void __launch_bounds__(kLayerThreads) layernorm_kernel(const float* x, const __half* g, const __half* b,
+                                                                  int d, float eps, __half* y, int ldy) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const float* xr = x + (size_t)m * d;
+  float v[PER];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    const int j = threadIdx.x + i * kLayerThreads;
+    v[i] = j < d ? xr[j] : 0.0f;
+    s += v[i];
+  }
+  const float mean = block_sum(s, red) / (float)d;
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    const int j = threadIdx.x + i * kLayerThreads;
+    const float c = j < d ? v[i] - mean : 0.0f;
+    q = fmaf(c, c, q);
+  }
+  const float var = block_sum(q, red) / (float)d;
+  const float rs = rsqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    const int j = threadIdx.x + i * kLayerThreads;
+    if (j < d) y[(size_t)m * ldy + j] = __float2half_rn((v[i] - mean) * rs * __half2float(g[j]) + __half2float(b[j]));
+  }
+}
+
+// One CTA per (sequence m, head hd).  qkv [M][3d] f16 holds this token's q, k,
+// v; the caches are f16 [M][max_seq][d].  The new k, v are written at pos[m]
+// first, then the scores of positions 0..pos[m] are computed (one position per
+// thread per pass, the head's q in shared memory), softmaxed in f32 and the
+// weighted sum of V formed with (thread = head dimension, positions split over
+// thread groups).  scores: shared memory of max_seq floats.
+__global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* qkv, int d, int dh, int max_seq,
+                                                                  const int* pos, __half* kc, __half* vc,
+                                                                  __half* out, float scale) {
+  extern __shared__ float sm[];  // [max_seq] scores, [dh] q, [kLayerThreads] partial sums
+  float* sc = sm;
+  float* qs = sm + max_seq;
+  float* part = qs + dh;
+  __shared__ float red[32];
+  const int m = blockIdx.x, hd = blockIdx.y, tid = threadIdx.x;
+  const int p = pos[m];
+  if (p < 0 || p >= max_seq) {  // no cache slot: the caller's position is out of range
+    for (int j = tid; j < dh; j += blockDim.x) out[(size_t)m * d + hd * dh + j] = __float2half_rn(0.0f);
+    return;
+  }
+  const __half* row = qkv + (size_t)m * 3 * d;
+  __half* kcm = kc + (size_t)m * max_seq * d + hd * dh;
+  __half* vcm = vc + (size_t)m * max_seq * d + hd * dh;
+  for (int j = tid; j < dh; j += blockDim.x) {
+    qs[j] = __half2float(row[hd * dh + j]);
+    kcm[(size_t)p * d + j] = row[d + hd * dh + j];
+    vcm[(size_t)p * d + j] = row[2 * d + hd * dh + j];
+  }
+  __syncthreads();  // the new k, v are in the cache (read back below by other threads)
+  const int n = p + 1;
+  float mx = -INFINITY;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kcm + (size_t)i * d);  // 8 halves per load
+    float dot = 0.0f;
+    for (int j = 0; j < dh / 8; j++) {
+      const uint4 w = kr[j];
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float2 kv = __half22float2(*reinterpret_cast<const __half2*>(&ws[u]));
+        dot = fmaf(qs[8 * j + 2 * u], kv.x, dot);
+        dot = fmaf(qs[8 * j + 2 * u + 1], kv.y, dot);
+      }
+    }
+    const float s = dot * scale;
+    sc[i] = s;
+    mx = fmaxf(mx, s);
+  }
+  mx = block_max(mx, red);
+  float sum = 0.0f;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float e = __expf(sc[i] - mx);
+    sc[i] = e;
+    sum += e;
+  }
+  sum = block_sum(sum, red);  // its barriers also publish sc[]
+  const float inv = 1.0f / sum;
+  // weighted sum of V: thread = (dimension j, position group pg)
+  const int groups = blockDim.x / dh;  // dh divides kLayerThreads (64 or 128 -> 4 or 2 groups)
+  const int j = tid % dh, pg = tid / dh;
+  float acc = 0.0f;
+  if (pg < groups)
+    for (int i = pg; i < n; i += groups) acc = fmaf(sc[i], __half2float(vcm[(size_t)i * d + j]), acc);
+  part[tid] = acc;
+  __syncthreads();
+  if (tid < dh) {
+    float o = 0.0f;
+    for (int g2 = 0; g2 < groups; g2++) o += part[g2 * dh + tid];
+    out[(size_t)m * d + hd * dh + tid] = __float2half_rn(o * inv);
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_embed(const __half* embed, const __half* pos_embed, const int* tok, const int* pos, int M, int vocab,
+                         int max_seq, int d, float* h, cudaStream_t st) {
+  embed_kernel<<<M, kLayerThreads, 0, st>>>(embed, pos_embed, tok, pos, vocab, max_seq, d, h);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm(const float* x, const __half* g, const __half* b, int M, int d, float eps, __half* y,
+                             int ldy, cudaStream_t st) {
+  const int per = (d + kLayerThreads - 1) / kLayerThreads;
+  if (per <= 4) layernorm_kernel<4><<<M, kLayerThreads, 0, st>>>(x, g, b, d, eps, y, ldy);
+  else if (per <= 16) layernorm_kernel<16><<<M, kLayerThreads, 0, st>>>(x, g, b, d, eps, y, ldy);
+  else layernorm_kernel<32><<<M, kLayerThreads, 0, st>>>(x, g, b, d, eps, y, ldy);
+  return cudaGetLastError();
+}
+
+size_t attention_smem_bytes(int dh, int max_seq) { return (size_t)(max_seq + dh + kLayerThreads) * sizeof(float); }
+
+cudaError_t launch_attention(const __half* qkv, int M, int d, int heads, int max_seq, const int* pos, __half* kc,
+                             __half* vc, __half* out, cudaStream_t st) {
+  const int dh = d / heads;
+  const size_t smem = attention_smem_bytes(dh, max_seq);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  attention_kernel<<<dim3(M, heads), kLayerThreads, smem, st>>>(qkv, d, dh, max_seq, pos, kc, vc, out,
+                                                                1.0f / sqrtf((float)dh));
+  return cudaGetLastError();
+}
+
+}  // namespace aria_q4

@@ -203,6 +203,39 @@ ARIA_Q4_API int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K,
                         void* y, int y_dtype, int ldy,
                         const uint16_t* bias, float alpha, float beta, int flags, void* stream);
 
+/* ---------------------------------------------------------------- decode step */
+
+/* The rest of a decode step with KV cache, around the projections above.  The
+ * reference runs its cached decode step on the CPU only (`step`,
+ * src/transformer_cuda.rs:1286-1324, over cpu_layer_forward :1059-1166); these
+ * kernels are its GPU counterparts.  The residual stream h is f32 [M][d] (the
+ * projections add into it with y_dtype = ARIA_Q4_F32 and beta = 1); activations
+ * fed to projections and the KV caches are f16. */
+
+/* h[m] = embed[tokens[m]] + pos_embed[positions[m]] (f16 tables [vocab][d],
+ * [max_seq][d]; f32 out), token and position clamped into the tables as the
+ * reference clamps them (:1290-1297).  tokens, positions: device int [M]. */
+ARIA_Q4_API int aria_embed_f16(const uint16_t* embed, const uint16_t* pos_embed, int vocab, int max_seq, int d,
+                               const int* tokens, const int* positions, int M, float* h, void* stream);
+
+/* y[m] = (x[m] - mean) / sqrt(var + eps) * gamma + beta over the d values of
+ * each f32 row, f16 out with row stride ldy (cpu_layernorm, :3271-3293; the
+ * reference uses eps = 1e-5).  d <= 8192. */
+ARIA_Q4_API int aria_layernorm_f32(const float* x, int M, int d, const uint16_t* gamma, const uint16_t* beta,
+                                   float eps, uint16_t* y, int ldy, void* stream);
+
+/* Single-token attention of M sequences (the attention block of
+ * cpu_layer_forward with t = 1, :1098-1137): qkv is f16 [M][3d] (q, k, v of the
+ * new token, heads of d / heads dimensions); its k and v are written into the
+ * caches (f16 [M][max_seq][d]) at positions[m] (device int [M]), then each
+ * head attends over positions 0..positions[m] with scale 1/sqrt(d / heads)
+ * and a max-subtracted softmax; out is f16 [M][d].  A position outside
+ * [0, max_seq) writes nothing to the caches and zeros to its output row.
+ * d / heads a multiple of 8 dividing 256; qkv and caches 16-byte aligned. */
+ARIA_Q4_API int aria_attention_decode(const uint16_t* qkv, int M, int d, int heads, uint16_t* k_cache,
+                                      uint16_t* v_cache, int max_seq, const int* positions, uint16_t* out,
+                                      void* stream);
+
 /* ---------------------------------------------------------------- errors */
 
 ARIA_Q4_API const char* aria_q4_strerror(int status);

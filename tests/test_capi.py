@@ -13,7 +13,7 @@ HEADER = os.path.join(ROOT, "include", "aria_q4.h")
 def declared_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(aria_q4\w*)\s*\(", text)))
+    return sorted(set(re.findall(r"\bARIA_Q4_API\s+[\w\s\*]*?\b(aria_\w*)\s*\(", text)))
 
 
 @pytest.fixture(scope="module")
