@@ -44,6 +44,7 @@ SIGNATURES = {
     "aria_q4_0_matmul_static_ws": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _F, _F, _I, _P]),
     "aria_q4_0_workspace_counter_bytes": (_SZ, []),
     "aria_q4_test_tensor_stall": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, ctypes.c_uint, _P]),
+    "aria_q4_0_matmul_ln": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _P, _F, _P, _I, _I, _P, _F, _F, _I, _P]),
     "aria_embed_f16": (_I, [_P, _P, _I, _I, _I, _P, _P, _I, _P, _P]),
     "aria_layernorm_f32": (_I, [_P, _I, _I, _P, _P, _F, _P, _I, _P]),
     "aria_attention_decode": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _P, _P]),

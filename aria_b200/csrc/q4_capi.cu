@@ -15,7 +15,8 @@ cudaError_t launch_repack(const uint8_t* blocks, int layout, int K, int N, uint8
 cudaError_t launch_quantize_tiled(const uint16_t* w, int layout, int K, int N, uint8_t* tiled, cudaStream_t st);
 cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                           int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
-                          bool const_weights);
+                          bool const_weights, const float* ln_h = nullptr, const __half* ln_g = nullptr,
+                          const __half* ln_b = nullptr, float ln_eps = 0.0f);
 bool gemv_supported(int K, int N, int M);
 cudaError_t launch_gemv(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                         int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
@@ -285,6 +286,29 @@ int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K, int N, cons
                              flags, stream);
 }
 
+// ------------------------------------------------------------------ LayerNorm prologue
+int aria_q4_0_matmul_ln(const void* tiled, int layout, int K, int N, const float* h, int M, int ldh,
+                        const uint16_t* gamma, const uint16_t* beta_ln, float eps, void* y, int y_dtype, int ldy,
+                        const uint16_t* bias, float alpha, float beta, int flags, void* stream) {
+  if (int s = check_tiled_shape(layout, K, N)) return s;
+  if (M < 0 || !(eps >= 0.0f)) return ARIA_Q4_EINVAL;
+  if (M == 0) return ARIA_Q4_OK;
+  if (!tiled || !h || !gamma || !beta_ln || !y) return ARIA_Q4_EINVAL;
+  if (y_dtype != ARIA_Q4_F16 && y_dtype != ARIA_Q4_F32) return ARIA_Q4_EINVAL;
+  if (ldh < K || ldy < N) return ARIA_Q4_EINVAL;
+  const int known = ARIA_Q4_FLAG_CONST_WEIGHTS | ARIA_Q4_FLAG_KERNEL_REGISTER | ARIA_Q4_FLAG_EPILOGUE_GELU;
+  if ((flags & ~known) != 0) return ARIA_Q4_EINVAL;
+  if (M > kDecodeMaxM) return ARIA_Q4_EUNSUPPORTED;
+  if (((uintptr_t)tiled & 255u) != 0 || !aligned16(h) || (ldh % 4) != 0 || !aligned16(gamma) || !aligned16(beta_ln))
+    return ARIA_Q4_EALIGN;
+  if (int s = check_device()) return s;
+  const int out = y_dtype | ((flags & ARIA_Q4_FLAG_EPILOGUE_GELU) ? aria_q4::kOutGelu : 0);
+  return cuda_status(launch_decode((const uint8_t*)tiled, layout, K, N, nullptr, M, ldh, y, out, ldy,
+                                   (const __half*)bias, alpha, beta, (cudaStream_t)stream, true,
+                                   (flags & ARIA_Q4_FLAG_CONST_WEIGHTS) != 0, h, (const __half*)gamma,
+                                   (const __half*)beta_ln, eps));
+}
+
 // ------------------------------------------------------------------ decode-step helpers
 int aria_embed_f16(const uint16_t* embed, const uint16_t* pos_embed, int vocab, int max_seq, int d,
                    const int* tokens, const int* positions, int M, float* h, void* stream) {
@@ -310,7 +334,7 @@ int aria_attention_decode(const uint16_t* qkv, int M, int d, int heads, uint16_t
                           int max_seq, const int* positions, uint16_t* out, void* stream) {
   if (M < 0 || d <= 0 || heads <= 0 || d % heads != 0 || max_seq <= 0) return ARIA_Q4_EINVAL;
   const int dh = d / heads;
-  if (dh % 8 != 0 || 256 % dh != 0) return ARIA_Q4_EUNSUPPORTED;
+  if (dh != 32 && dh != 64 && dh != 128 && dh != 256) return ARIA_Q4_EUNSUPPORTED;
   if (attention_smem_bytes(dh, max_seq) > 227 * 1024) return ARIA_Q4_EUNSUPPORTED;
   if (M == 0) return ARIA_Q4_OK;
   if (!qkv || !k_cache || !v_cache || !positions || !out) return ARIA_Q4_EINVAL;

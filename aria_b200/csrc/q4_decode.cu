@@ -51,6 +51,12 @@ struct DecodeArgs {
   int ksplit;  // warps per 16-row tile (within a CTA)
   int csplit;  // CTAs per tile group (a thread-block cluster along x)
   int const_weights;  // weights are not written by the preceding kernel: load them before the dependency wait
+  // LayerNorm prologue (h != nullptr): x = LayerNorm(h) rounded to f16, with h
+  // f32 [M][ldx], per-k gain / shift ln_g, ln_b (f16 [K]) and ln_eps; x unused
+  const float* h;
+  const __half* ln_g;
+  const __half* ln_b;
+  float ln_eps;
 };
 
 __device__ __forceinline__ uint4 ld_u4_or(const void* p, bool ok, uint32_t fill) {
@@ -70,9 +76,12 @@ struct GroupRegs {
 
 // PRE: the batch phase also loads every activation / KN-scale fragment of its
 // groups (small NT), so no load latency is exposed inside the MMA loop.
-template <int LAYOUT, int NT, int MAXB, bool PRE>
+// LN: the LayerNorm prologue (a separate instance, so that the plain kernel
+// keeps its register budget).
+template <int LAYOUT, int NT, int MAXB, bool PRE, bool LN>
 __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) {
   __shared__ float red[8][32][NT * 4];
+  __shared__ float2 ln_stat[8 * NT];  // LayerNorm prologue: (mean, rstd) of this CTA's token rows
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int S = a.ksplit, C = a.csplit;
@@ -103,8 +112,28 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
   const int grp = r0 >> 5;  // 32-row scale group (KN)
   auto load_x = [&](int kb, int j) -> uint4 {
     const int tok = m0 + 8 * j + g;
-    return (tok < a.M && kb < a.K) ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)tok * a.ldx + kb + 8 * t))
-                                   : make_uint4(0, 0, 0, 0);
+    if (tok >= a.M || kb >= a.K) return make_uint4(0, 0, 0, 0);
+    if (!LN) return __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)tok * a.ldx + kb + 8 * t));
+    // LayerNorm of the f32 row, (v - mean) * rstd * g + b as the LayerNorm
+    // kernel computes it, rounded to f16 as that kernel would store it
+    const float* hp = a.h + (size_t)tok * a.ldx + kb + 8 * t;
+    const float4 h0 = __ldg(reinterpret_cast<const float4*>(hp));
+    const float4 h1 = __ldg(reinterpret_cast<const float4*>(hp + 4));
+    const uint4 gw = __ldg(reinterpret_cast<const uint4*>(a.ln_g + kb + 8 * t));
+    const uint4 bw = __ldg(reinterpret_cast<const uint4*>(a.ln_b + kb + 8 * t));
+    const float2 st = ln_stat[tok - m0];
+    const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const uint32_t gs[4] = {gw.x, gw.y, gw.z, gw.w}, bs[4] = {bw.x, bw.y, bw.z, bw.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const float2 gf = __half22float2(*reinterpret_cast<const __half2*>(&gs[u]));
+      const float2 bf = __half22float2(*reinterpret_cast<const __half2*>(&bs[u]));
+      const __half2 r = __floats2half2_rn((hv[2 * u] - st.x) * st.y * gf.x + bf.x,
+                                          (hv[2 * u + 1] - st.x) * st.y * gf.y + bf.y);
+      o[u] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
   };
   auto load_ks = [&](int kb) -> uint4 {
     return (active_warp && kb < a.Kp) ? __ldg(reinterpret_cast<const uint4*>(a.scales + (size_t)grp * a.Kp + kb + 8 * t))
@@ -155,6 +184,30 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
   }
   grid_dep_launch();
   grid_dep_wait();
+
+  if (LN) {
+    // LayerNorm statistics of this CTA's token rows, one warp per row: the
+    // mean, then the mean of the centred squares (two passes, as the
+    // reference's cpu_layernorm_stats, lold3344/ARIA src/transformer_cuda.rs:3276-3293)
+    const int nrow = min(8 * NT, a.M - m0);
+    for (int tl = warp; tl < nrow; tl += 8) {
+      const float* hr = a.h + (size_t)(m0 + tl) * a.ldx;
+      float sum = 0.0f;
+      for (int k = lane; k < a.K; k += 32) sum += hr[k];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float mean = sum / (float)a.K;
+      float sq = 0.0f;
+      for (int k = lane; k < a.K; k += 32) {
+        const float c = hr[k] - mean;
+        sq = fmaf(c, c, sq);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      if (lane == 0) ln_stat[tl] = make_float2(mean, rsqrtf(sq / (float)a.K + a.ln_eps));
+    }
+    __syncthreads();
+  }
 
   if (active_warp) {
     for (int gb = gbeg; gb < gend; gb += MAXB) {
@@ -273,8 +326,8 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
       [&](int i) { return tok(i) < a.M && ((i & 3) >= 2 ? okb : oka); });
 }
 
-template <int LAYOUT, int NT, int MAXB, bool PRE>
-static cudaError_t launch_t(const DecodeArgs& a, cudaStream_t st, bool pdl) {
+template <int LAYOUT, int NT, int MAXB, bool PRE, bool LN>
+static cudaError_t launch_t2(const DecodeArgs& a, cudaStream_t st, bool pdl) {
   const int tiles = (a.N + 15) / 16;
   const int tpc = 8 / a.ksplit;
   dim3 grid(((tiles + tpc - 1) / tpc) * a.csplit, (a.M + 8 * NT - 1) / (8 * NT));
@@ -299,7 +352,13 @@ static cudaError_t launch_t(const DecodeArgs& a, cudaStream_t st, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<LAYOUT, NT, MAXB, PRE>, a);
+  return cudaLaunchKernelEx(&cfg, decode_mma_kernel<LAYOUT, NT, MAXB, PRE, LN>, a);
+}
+
+template <int LAYOUT, int NT, int MAXB, bool PRE>
+static cudaError_t launch_t(const DecodeArgs& a, cudaStream_t st, bool pdl) {
+  if (a.h) return launch_t2<LAYOUT, NT, MAXB, PRE, true>(a, st, pdl);
+  return launch_t2<LAYOUT, NT, MAXB, PRE, false>(a, st, pdl);
 }
 
 template <int LAYOUT>
@@ -319,9 +378,14 @@ static cudaError_t launch_layout(const DecodeArgs& a, int nt, int gpw, cudaStrea
 // reduces through distributed shared memory.
 cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const __half* x, int M, int ldx, void* y,
                           int ydt, int ldy, const __half* bias, float alpha, float beta, cudaStream_t st, bool pdl,
-                          bool const_weights) {
+                          bool const_weights, const float* ln_h, const __half* ln_g, const __half* ln_b,
+                          float ln_eps) {
   DecodeArgs a;
   a.const_weights = const_weights ? 1 : 0;
+  a.h = ln_h;
+  a.ln_g = ln_g;
+  a.ln_b = ln_b;
+  a.ln_eps = ln_eps;
   a.qs = tiled;
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
   a.K = K; a.N = N; a.Kp = padded_k(K);

@@ -96,43 +96,51 @@ __global__ void __launch_bounds__(kLayerThreads) layernorm_kernel(const float* x
   }
 }
 
-// One CTA per (sequence m, head hd).  qkv [M][3d] f16 holds this token's q, k,
-// v; the caches are f16 [M][max_seq][d].  The new k, v are written at pos[m]
-// first, then the scores of positions 0..pos[m] are computed (one position per
-// thread per pass, the head's q in shared memory), softmaxed in f32 and the
-// weighted sum of V formed with (thread = head dimension, positions split over
-// thread groups).  scores: shared memory of max_seq floats.
-__global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* qkv, int d, int dh, int max_seq,
+// One CTA per (sequence m, head hd), head dimension DH.  qkv [M][3d] f16 holds
+// this token's q, k, v; the caches are f16 [M][max_seq][d].  The new k, v are
+// written at pos[m] first; then every thread scores whole positions (the k
+// row's DH/8 16-byte loads issued before the first multiply, q in shared
+// memory), the scores are softmaxed in f32 (max-subtracted), and the weighted
+// sum of V is formed by (head dimension pair, position group) threads, 16
+// positions' values loaded before their multiply-adds.  Loads are batched
+// because a load feeding the next multiply-add of a chain would otherwise
+// wait out one memory round trip per cached position.  scores: shared memory
+// of max_seq floats.
+template <int DH>
+__global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* qkv, int d, int max_seq,
                                                                   const int* pos, __half* kc, __half* vc,
                                                                   __half* out, float scale) {
-  extern __shared__ float sm[];  // [max_seq] scores, [dh] q, [kLayerThreads] partial sums
+  extern __shared__ float sm[];  // [max_seq] scores, [DH] q, [2 kLayerThreads] partial sums
   float* sc = sm;
   float* qs = sm + max_seq;
-  float* part = qs + dh;
+  float* part = qs + DH;
   __shared__ float red[32];
   const int m = blockIdx.x, hd = blockIdx.y, tid = threadIdx.x;
   const int p = pos[m];
   if (p < 0 || p >= max_seq) {  // no cache slot: the caller's position is out of range
-    for (int j = tid; j < dh; j += blockDim.x) out[(size_t)m * d + hd * dh + j] = __float2half_rn(0.0f);
+    for (int j = tid; j < DH; j += blockDim.x) out[(size_t)m * d + hd * DH + j] = __float2half_rn(0.0f);
     return;
   }
   const __half* row = qkv + (size_t)m * 3 * d;
-  __half* kcm = kc + (size_t)m * max_seq * d + hd * dh;
-  __half* vcm = vc + (size_t)m * max_seq * d + hd * dh;
-  for (int j = tid; j < dh; j += blockDim.x) {
-    qs[j] = __half2float(row[hd * dh + j]);
-    kcm[(size_t)p * d + j] = row[d + hd * dh + j];
-    vcm[(size_t)p * d + j] = row[2 * d + hd * dh + j];
+  __half* kcm = kc + (size_t)m * max_seq * d + hd * DH;
+  __half* vcm = vc + (size_t)m * max_seq * d + hd * DH;
+  for (int j = tid; j < DH; j += blockDim.x) {
+    qs[j] = __half2float(row[hd * DH + j]);
+    kcm[(size_t)p * d + j] = row[d + hd * DH + j];
+    vcm[(size_t)p * d + j] = row[2 * d + hd * DH + j];
   }
   __syncthreads();  // the new k, v are in the cache (read back below by other threads)
   const int n = p + 1;
   float mx = -INFINITY;
   for (int i = tid; i < n; i += blockDim.x) {
     const uint4* kr = reinterpret_cast<const uint4*>(kcm + (size_t)i * d);  // 8 halves per load
+    uint4 kw[DH / 8];
+#pragma unroll
+    for (int j = 0; j < DH / 8; j++) kw[j] = kr[j];
     float dot = 0.0f;
-    for (int j = 0; j < dh / 8; j++) {
-      const uint4 w = kr[j];
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < DH / 8; j++) {
+      const uint32_t ws[4] = {kw[j].x, kw[j].y, kw[j].z, kw[j].w};
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const float2 kv = __half22float2(*reinterpret_cast<const __half2*>(&ws[u]));
@@ -153,18 +161,40 @@ __global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* 
   }
   sum = block_sum(sum, red);  // its barriers also publish sc[]
   const float inv = 1.0f / sum;
-  // weighted sum of V: thread = (dimension j, position group pg)
-  const int groups = blockDim.x / dh;  // dh divides kLayerThreads (64 or 128 -> 4 or 2 groups)
-  const int j = tid % dh, pg = tid / dh;
-  float acc = 0.0f;
-  if (pg < groups)
-    for (int i = pg; i < n; i += groups) acc = fmaf(sc[i], __half2float(vcm[(size_t)i * d + j]), acc);
-  part[tid] = acc;
+  // weighted sum of V: thread = (dimension pair jp, position group pg); up to
+  // 16 positions' pairs loaded before their multiply-adds
+  constexpr int kPairs = DH / 2, kGroups = kLayerThreads / kPairs;
+  const int jp = tid % kPairs, pg = tid / kPairs;
+  float ax = 0.0f, ay = 0.0f;
+  int i = pg;
+  for (; i + 15 * kGroups < n; i += 16 * kGroups) {
+    __half2 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) v[u] = *reinterpret_cast<const __half2*>(vcm + (size_t)(i + u * kGroups) * d + 2 * jp);
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+      const float2 f = __half22float2(v[u]);
+      const float w = sc[i + u * kGroups];
+      ax = fmaf(w, f.x, ax);
+      ay = fmaf(w, f.y, ay);
+    }
+  }
+  for (; i < n; i += kGroups) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vcm + (size_t)i * d + 2 * jp));
+    ax = fmaf(sc[i], f.x, ax);
+    ay = fmaf(sc[i], f.y, ay);
+  }
+  part[2 * tid] = ax;
+  part[2 * tid + 1] = ay;
   __syncthreads();
-  if (tid < dh) {
-    float o = 0.0f;
-    for (int g2 = 0; g2 < groups; g2++) o += part[g2 * dh + tid];
-    out[(size_t)m * d + hd * dh + tid] = __float2half_rn(o * inv);
+  if (tid < kPairs) {
+    float ox = 0.0f, oy = 0.0f;
+#pragma unroll
+    for (int g2 = 0; g2 < kGroups; g2++) {
+      ox += part[2 * (g2 * kPairs + tid)];
+      oy += part[2 * (g2 * kPairs + tid) + 1];
+    }
+    *reinterpret_cast<__half2*>(out + (size_t)m * d + hd * DH + 2 * tid) = __floats2half2_rn(ox * inv, oy * inv);
   }
 }
 
@@ -184,19 +214,28 @@ cudaError_t launch_layernorm(const float* x, const __half* g, const __half* b, i
   return cudaGetLastError();
 }
 
-size_t attention_smem_bytes(int dh, int max_seq) { return (size_t)(max_seq + dh + kLayerThreads) * sizeof(float); }
+size_t attention_smem_bytes(int dh, int max_seq) { return (size_t)(max_seq + dh + 2 * kLayerThreads) * sizeof(float); }
 
 cudaError_t launch_attention(const __half* qkv, int M, int d, int heads, int max_seq, const int* pos, __half* kc,
                              __half* vc, __half* out, cudaStream_t st) {
   const int dh = d / heads;
   const size_t smem = attention_smem_bytes(dh, max_seq);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+  const float scale = 1.0f / sqrtf((float)dh);
+  auto run = [&](auto kern) -> cudaError_t {
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    kern<<<dim3(M, heads), kLayerThreads, smem, st>>>(qkv, d, max_seq, pos, kc, vc, out, scale);
+    return cudaGetLastError();
+  };
+  switch (dh) {
+    case 32: return run(attention_kernel<32>);
+    case 64: return run(attention_kernel<64>);
+    case 128: return run(attention_kernel<128>);
+    case 256: return run(attention_kernel<256>);
+    default: return cudaErrorInvalidValue;
   }
-  attention_kernel<<<dim3(M, heads), kLayerThreads, smem, st>>>(qkv, d, dh, max_seq, pos, kc, vc, out,
-                                                                1.0f / sqrtf((float)dh));
-  return cudaGetLastError();
 }
 
 }  // namespace aria_q4

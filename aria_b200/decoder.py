@@ -7,14 +7,15 @@ every operation runs on the GPU through libaria_q4.so:
 
     h  = embed[token] + pos_embed[pos]                      aria_embed_f16
     per layer:
-      xn = LayerNorm1(h)                                    aria_layernorm_f32
-      qkv = xn @ w_qkv + b_qkv                              aria_q4_0_matmul_ws (Q4_0)
+      qkv = LayerNorm1(h) @ w_qkv + b_qkv                   aria_q4_0_matmul_ln (LayerNorm prologue)
       att = attention(q; K, V cache with this k, v added)   aria_attention_decode
-      h  += att @ w_out + b_out                             (beta = 1 into the f32 residual)
-      xn = LayerNorm2(h)
-      u  = GELU(xn @ w_ff1 + b_ff1)                         (GELU fused in the epilogue)
+      h  += att @ w_out + b_out                             aria_q4_0_matmul_ws, beta = 1 into the f32 residual
+      u  = GELU(LayerNorm2(h) @ w_ff1 + b_ff1)              aria_q4_0_matmul_ln, GELU in the epilogue
       h  += u @ w_ff2 + b_ff2
-    logits = LayerNorm_f(h) @ embed^T                       (tied LM head, Q4_0)
+    logits = LayerNorm_f(h) @ embed^T                       aria_layernorm_f32 + the tied LM head (Q4_0)
+
+(above 64 sequences the LayerNorms run as aria_layernorm_f32 launches before
+the projections).
 
 The residual stream h is f32; the LayerNorm outputs, q/k/v, the attention
 output, the FFN hidden activation and the caches are f16 (the activation type
@@ -35,7 +36,7 @@ import torch
 from . import _lib
 from ._lib import call
 from .efkolos import EfkolosConfig, synth_f16
-from .q4 import LAYOUT_KN, LAYOUT_NK, Q4Weight, matmul
+from .q4 import LAYOUT_KN, LAYOUT_NK, Q4Weight, matmul, matmul_ln
 
 LN_EPS = 1e-5  # cpu_layernorm_stats (:3277)
 
@@ -146,15 +147,23 @@ class Decoder:
         d = cfg.d_model
         call("aria_embed_f16", w.embed.data_ptr(), w.pos_embed.data_ptr(), cfg.vocab_size, w.max_seq, d,
              self.tokens.data_ptr(), self.positions.data_ptr(), self.M, self.h.data_ptr(), _stream())
+        fused_ln = self.M <= 64  # LayerNorm as the prologue of QKV / ffn_up (register-fed kernel)
         for i, p in enumerate(w.layers):
-            self._layernorm(p.ln1_g, p.ln1_b)
-            matmul(self.xn, p.qkv, self.qkv, bias=p.b_qkv, const_weights=True)
+            if fused_ln:
+                matmul_ln(self.h, p.ln1_g, p.ln1_b, p.qkv, self.qkv, eps=LN_EPS, bias=p.b_qkv, const_weights=True)
+            else:
+                self._layernorm(p.ln1_g, p.ln1_b)
+                matmul(self.xn, p.qkv, self.qkv, bias=p.b_qkv, const_weights=True)
             call("aria_attention_decode", self.qkv.data_ptr(), self.M, d, cfg.num_heads,
                  self.k_cache[i].data_ptr(), self.v_cache[i].data_ptr(), w.max_seq, self.positions.data_ptr(),
                  self.att.data_ptr(), _stream())
             matmul(self.att, p.out, self.h, bias=p.b_out, beta=1.0, const_weights=True)
-            self._layernorm(p.ln2_g, p.ln2_b)
-            matmul(self.xn, p.up, self.u, bias=p.b_up, activation="gelu", const_weights=True)
+            if fused_ln:
+                matmul_ln(self.h, p.ln2_g, p.ln2_b, p.up, self.u, eps=LN_EPS, bias=p.b_up, activation="gelu",
+                          const_weights=True)
+            else:
+                self._layernorm(p.ln2_g, p.ln2_b)
+                matmul(self.xn, p.up, self.u, bias=p.b_up, activation="gelu", const_weights=True)
             matmul(self.u, p.down, self.h, bias=p.b_down, beta=1.0, const_weights=True)
         self._layernorm(w.lnf_g, w.lnf_b)
         matmul(self.xn, w.head, self.logits, const_weights=True)
@@ -170,7 +179,7 @@ class Decoder:
 
     @property
     def launches(self) -> int:
-        return 1 + 7 * self.cfg.num_layers + 2
+        return 1 + (5 if self.M <= 64 else 7) * self.cfg.num_layers + 2
 
 
 __all__ = ["Decoder", "DecoderWeights", "sinusoidal_positions", "LN_EPS"]

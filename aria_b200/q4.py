@@ -20,7 +20,7 @@ import torch
 from . import _lib
 from ._lib import F16, F32, LAYOUT_KN, LAYOUT_NK, call
 
-__all__ = ["quantize_q4_0", "packed_bytes", "dequantize_q4_0", "Q4Weight", "gemm_q4", "matmul",
+__all__ = ["quantize_q4_0", "packed_bytes", "dequantize_q4_0", "Q4Weight", "gemm_q4", "matmul", "matmul_ln",
            "LAYOUT_KN", "LAYOUT_NK"]
 
 
@@ -201,6 +201,28 @@ def matmul(x: torch.Tensor, w: Q4Weight, out: torch.Tensor | None = None, *, bia
          workspace.numel() * workspace.element_size() if workspace is not None else 0,
          (_lib.FLAG_CONST_WEIGHTS if const_weights else 0) | _KERNEL_FLAGS[kernel] | _ACT_FLAGS[activation],
          _stream(x.device))
+    return out
+
+
+def matmul_ln(h: torch.Tensor, gamma: torch.Tensor, beta_ln: torch.Tensor, w: Q4Weight,
+              out: torch.Tensor | None = None, *, eps: float = 1e-5, bias: torch.Tensor | None = None,
+              beta: float = 0.0, out_dtype: torch.dtype = torch.float16, const_weights: bool = False,
+              activation: str | None = None) -> torch.Tensor:
+    """y = act(LayerNorm(h) @ W + bias) + beta * out through aria_q4_0_matmul_ln:
+    the reference's LayerNorm followed by a projection (cpu_layer_forward,
+    src/transformer_cuda.rs:1092-1096, :1145-1150) in one launch.  h is f32
+    [M, K] (M <= 64), gamma / beta_ln f16 [K]."""
+    _require_cuda(h, "h")
+    if h.dtype != torch.float32 or h.dim() != 2 or h.shape[1] != w.K:
+        raise ValueError("h must be f32 [M, K]")
+    M = h.shape[0]
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype, device=h.device)
+    ydt = {torch.float16: F16, torch.float32: F32}[out.dtype]
+    call("aria_q4_0_matmul_ln", w.buf.data_ptr(), w.layout, w.K, w.N, h.data_ptr(), M, h.stride(0),
+         gamma.data_ptr(), beta_ln.data_ptr(), float(eps), out.data_ptr(), ydt, out.stride(0),
+         bias.data_ptr() if bias is not None else None, 1.0, float(beta),
+         (_lib.FLAG_CONST_WEIGHTS if const_weights else 0) | _ACT_FLAGS[activation], _stream(h.device))
     return out
 
 

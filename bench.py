@@ -370,6 +370,45 @@ def flags_for(kernel: str) -> int:
             "tensor": _lib.FLAG_KERNEL_TENSOR}[kernel]
 
 
+def decode_kv_section(rank, world, stream, timed, steps: int) -> dict:
+    """The whole decode step with KV cache on the GPU (aria_b200.decoder: the
+    reference's cached `step`, src/transformer_cuda.rs:1286-1324, with LayerNorm,
+    attention over the cache and the Q4_0 projections), Efkolos config, one new
+    token per sequence at position 255 (256 positions attended), M = 1 and 16
+    sequences.  Caches hold random f16 keys and values."""
+    import torch
+    from aria_b200.decoder import Decoder, DecoderWeights
+    from aria_b200.efkolos import EFKOLOS
+    w = DecoderWeights(EFKOLOS, max_seq=512, seed=rank + 3)
+    out = {"workload": "Efkolos decode step with KV cache (LayerNorm, QKV, attention over 256 cached positions, "
+                       "attn_out, LayerNorm, ffn_up+GELU, ffn_down, final LayerNorm, LM head)",
+           "q4_weight_bytes": w.q4_bytes}
+    for M in (1, 16):
+        dec = Decoder(w, M=M)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(rank + M)
+        for kc, vc in zip(dec.k_cache, dec.v_cache):
+            kc.copy_(torch.randn(kc.shape, generator=gen, device="cuda", dtype=torch.float16))
+            vc.copy_(torch.randn(vc.shape, generator=gen, device="cuda", dtype=torch.float16))
+        dec.tokens.copy_(torch.arange(M, dtype=torch.int32) * 997 % EFKOLOS.vocab_size)
+        dec.positions.fill_(255)
+        with torch.cuda.stream(stream):
+            dec.run()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                dec.run()
+        n = max(10, steps // 4)
+        ms = timed(lambda i: g.replay(), n, 3, f"aria_decode_kv_M{M}") / n
+        out[f"M{M}"] = {"ms_per_step": ms, "tokens_per_s": M * world / (ms * 1e-3), "context_positions": 256,
+                        "launches_per_step": dec.launches,
+                        "q4_weight_GBs": w.q4_bytes * world / (ms * 1e-3) / 1e9}
+        del g, dec
+    del w
+    torch.cuda.empty_cache()
+    return out
+
+
 def kernel_name(w, M: int, flags: int = 0, workspace_bytes: int = 0) -> str:
     """The kernel the library routes this projection to (aria_q4_0_kernel_choice)."""
     from aria_b200._lib import lib
@@ -661,6 +700,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                             "frac_of_measured_sustained_peak": tf / world / bf16_sus}
         del g, pprog
         torch.cuda.empty_cache()
+    decode_kv = decode_kv_section(rank, world, stream, timed, args.steps)
     cublas = None
     if rank == 0 and world == 1 and not args.no_cublas:
         cublas = cublas_fp16_section(stream, timed, l2, ms_step,
@@ -689,6 +729,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                    "tokens (8x512 = 4096, 4x2048 = 8192), tcgen05 kernel",
                        "flops_per_token": flops_token, "peak_tflops_measured": bf16_peak,
                        "peak_tflops_sustained": bf16_sus, **prefill},
+           "decode_step_kv": decode_kv,
            "scaled": scaled,
            "gemv_config4_b1": gemv_large,
            "cublas_fp16_same_box": cublas,

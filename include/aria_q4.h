@@ -212,6 +212,21 @@ ARIA_Q4_API int aria_q4_0_matmul_static_ws(const void* tiled, int layout, int K,
  * projections add into it with y_dtype = ARIA_Q4_F32 and beta = 1); activations
  * fed to projections and the KV caches are f16. */
 
+/* aria_q4_0_matmul_ex with the reference's LayerNorm as its prologue:
+ *     y = act(alpha * LayerNorm(h) . W + bias) + beta * y
+ * where LayerNorm(h) = (h - mean) / sqrt(var + eps) * gamma + beta_ln per f32
+ * row of h [M][ldh] (two-pass statistics, rounded once to f16 -- the value a
+ * separate LayerNorm would store for the projection to read).  Replaces the
+ * reference's LayerNorm + gemm pairs before QKV and ffn_up (cpu_layer_forward
+ * :1092-1096 and :1145-1150; LayerNorm :3271-3293, eps 1e-5) in one launch.
+ * Runs the register-fed decode kernel: M <= 64; flags: CONST_WEIGHTS,
+ * KERNEL_REGISTER, EPILOGUE_GELU.  h 16-byte aligned with ldh % 4 == 0;
+ * gamma, beta_ln f16 [K], 16-byte aligned. */
+ARIA_Q4_API int aria_q4_0_matmul_ln(const void* tiled, int layout, int K, int N, const float* h, int M, int ldh,
+                                    const uint16_t* gamma, const uint16_t* beta_ln, float eps,
+                                    void* y, int y_dtype, int ldy, const uint16_t* bias, float alpha, float beta,
+                                    int flags, void* stream);
+
 /* h[m] = embed[tokens[m]] + pos_embed[positions[m]] (f16 tables [vocab][d],
  * [max_seq][d]; f32 out), token and position clamped into the tables as the
  * reference clamps them (:1290-1297).  tokens, positions: device int [M]. */
@@ -231,7 +246,7 @@ ARIA_Q4_API int aria_layernorm_f32(const float* x, int M, int d, const uint16_t*
  * head attends over positions 0..positions[m] with scale 1/sqrt(d / heads)
  * and a max-subtracted softmax; out is f16 [M][d].  A position outside
  * [0, max_seq) writes nothing to the caches and zeros to its output row.
- * d / heads a multiple of 8 dividing 256; qkv and caches 16-byte aligned. */
+ * d / heads one of 32, 64, 128, 256; qkv and caches 16-byte aligned. */
 ARIA_Q4_API int aria_attention_decode(const uint16_t* qkv, int M, int d, int heads, uint16_t* k_cache,
                                       uint16_t* v_cache, int max_seq, const int* positions, uint16_t* out,
                                       void* stream);

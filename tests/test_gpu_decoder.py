@@ -94,6 +94,37 @@ def test_embed_kernel_clamps():
     assert np.array_equal(h.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("layout,K,N,M", [(0, 896, 2688, 1), (0, 896, 3584, 5), (0, 4096, 1024, 16),
+                                          (1, 896, 1000, 40), (0, 256, 512, 64)])
+def test_layernorm_prologue(coracle, layout, K, N, M):
+    """aria_q4_0_matmul_ln against the fp64 oracle of LayerNorm (rounded to f16,
+    as the projection reads it) followed by the projection, with bias and the
+    GELU epilogue; and against the separate LayerNorm kernel + projection."""
+    from aria_b200 import _lib, q4
+    from oracle.decode_step_np import f16, layernorm
+    from oracle.q4_oracle_np import gelu_tanh
+    rng = np.random.default_rng(K + N + M)
+    h = (rng.standard_normal((M, K)) * 2 + 0.3).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    b = (0.1 * rng.standard_normal(K)).astype(np.float16)
+    bias = (0.05 * rng.standard_normal(N)).astype(np.float16)
+    shape = (K, N) if layout == 0 else (N, K)
+    w = (rng.standard_normal(shape) * 0.02).astype(np.float16)
+    blocks = coracle.quantize_q4_0_f16(w.reshape(-1))
+    wq = q4.Q4Weight.from_f16(torch.from_numpy(w).cuda(), layout)
+    ht, gt, bt, biast = (torch.from_numpy(a).cuda() for a in (h, g, b, bias))
+    y = q4.matmul_ln(ht, gt, bt, wq, bias=biast, out_dtype=torch.float32, activation="gelu")
+    xn = torch.empty(M, K, dtype=torch.float16, device="cuda")
+    _lib.call("aria_layernorm_f32", ht.data_ptr(), M, K, gt.data_ptr(), bt.data_ptr(), 1e-5, xn.data_ptr(), K,
+              _stream())
+    y2 = q4.matmul(xn, wq, bias=biast, out_dtype=torch.float32, activation="gelu", kernel="register")
+    torch.cuda.synchronize()
+    xref = f16(layernorm(h, g.astype(np.float64), b.astype(np.float64)))
+    ref = gelu_tanh(coracle.matmul_ref(blocks, layout, K, N, xref.astype(np.float16), bias))
+    check_close(y.cpu().numpy(), ref, what=f"LayerNorm prologue {layout} {K}x{N} M={M}")
+    check_close(y.cpu().numpy(), y2.cpu().numpy().astype(np.float64), what="prologue vs separate LayerNorm")
+
+
 def _oracle_params(w):
     p = {k: v.cpu().numpy() for k, v in w.f16.items()}
     for i, lp in enumerate(w.layers):
