@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--launches", type=int, default=3, help="--case: launches before exiting")
     ap.add_argument("--kernel", default="auto", help="--case: auto, stream, register or tensor")
     ap.add_argument("--time", action="store_true", help="--case: also time the kind over weight copies")
+    ap.add_argument("--program", default=None, choices=["decode_step", "decode_kv"],
+                    help="run one whole program --launches times (for ncu launch lists): the 81-projection "
+                         "step (decode_step, --M token rows) or the decode step with KV cache (decode_kv)")
     return ap.parse_args()
 
 
@@ -265,6 +268,28 @@ def case_shape(name: str):
         if n.endswith(base) or n == base:
             return lay, K, N, s
     raise SystemExit(f"unknown case {name}")
+
+
+def run_program(args) -> None:
+    """A whole step, --launches times, on fresh seeded weights (for ncu launch
+    lists of the kernels a step runs and their shares)."""
+    import torch
+    from aria_b200.efkolos import EFKOLOS, DecodeProgram, Q4Stack
+    if args.program == "decode_step":
+        prog = DecodeProgram(Q4Stack.build(EFKOLOS, seed=1), M=args.M, seed=2)
+        run = prog.run
+    else:
+        from aria_b200.decoder import Decoder, DecoderWeights
+        dec = Decoder(DecoderWeights(EFKOLOS, max_seq=512, seed=3), M=args.M)
+        dec.positions.fill_(255)
+        run = dec.run
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("aria_program")
+    for _ in range(args.launches):
+        run()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(json.dumps({"program": args.program, "M": args.M, "runs": args.launches}), flush=True)
 
 
 def run_case(args) -> None:
@@ -752,6 +777,9 @@ def main():
         return
     if args.case:
         run_case(args)
+        return
+    if args.program:
+        run_program(args)
         return
     if world > 1:
         import datetime
