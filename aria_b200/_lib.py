@@ -48,6 +48,8 @@ SIGNATURES = {
     "aria_embed_f16": (_I, [_P, _P, _I, _I, _I, _P, _P, _I, _P, _P]),
     "aria_layernorm_f32": (_I, [_P, _I, _I, _P, _P, _F, _P, _I, _P]),
     "aria_attention_decode": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _P, _P]),
+    "aria_flash_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P]),
+    "aria_attention_prefill": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),
     "aria_q4_strerror": (ctypes.c_char_p, [_I]),
     "aria_q4_last_cuda_error": (_I, []),
     "aria_q4_take_device_error": (_I, []),

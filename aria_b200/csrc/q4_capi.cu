@@ -29,6 +29,10 @@ size_t tc_workspace_bytes(int K, int N, int M);
 size_t tc_workspace_used(int K, int N, int M, size_t ws_avail);
 size_t tc_workspace_counter_bytes();
 int take_device_error();
+int attn_take_device_error();
+cudaError_t launch_attention_prefill(const __half* q, const __half* k, const __half* v, int DH, long long s_head,
+                                     long long s_pos, long long s_seq, int B, int H, int T, float scale, __half* out,
+                                     long long o_seq, long long o_head, long long o_pos, float* lse, cudaStream_t st);
 cudaError_t launch_embed(const __half* embed, const __half* pos_embed, const int* tok, const int* pos, int M, int vocab,
                          int max_seq, int d, float* h, cudaStream_t st);
 cudaError_t launch_layernorm(const float* x, const __half* g, const __half* b, int M, int d, float eps, __half* y,
@@ -53,6 +57,7 @@ static const int kDecodeMaxM = ARIA_Q4_DECODE_MAX_M;
 // CTAs, overlaps better with its neighbours in a chain of projections.
 static const double kStreamMinBytesPerSm = 32.0 * 1024;
 static const int kStreamMinK = 2048;
+static const int kRegisterMaxN = 1024;
 static bool stream_by_default(int K, int N, int M) {
   if (M > 8) return false;
   const double per_sm = (double)N * (aria_q4::padded_k(K) / 128) * 72.0 / 148.0;
@@ -145,11 +150,14 @@ int aria_q4_0_quantize_tiled(const uint16_t* w, int layout, int K, int N, void* 
 }
 
 // Kernel choice: the streaming GEMV for M <= 8 and large weights; the
-// register-fed decode kernel up to 32 tokens; the tcgen05 kernel above that
-// (splitting K through the workspace when tiles are few), except without a
-// workspace for the shapes it would have split (the register-fed kernel splits
-// K itself, up to 64 tokens).  ARIA_Q4_FLAG_KERNEL_* overrides the choice.
-// Returns an ARIA_Q4_KERNEL_* value, or a negated status.
+// register-fed decode kernel up to 32 tokens, and up to 64 when the weight has
+// at most kRegisterMaxN outputs (few row tiles: its 16-token passes beat the
+// tcgen05 kernel's fixed cost; measured on B200 in chains at M = 64: Efkolos
+// attn_out 2.8 against 6.5 us, ffn_down 10.3 against 12.4 us); the tcgen05
+// kernel above that (splitting K through the workspace when tiles are few),
+// except without a workspace for the shapes it would have split (the
+// register-fed kernel splits K itself).  ARIA_Q4_FLAG_KERNEL_* overrides the
+// choice.  Returns an ARIA_Q4_KERNEL_* value, or a negated status.
 static int choose_kernel(int K, int N, int M, bool has_workspace, int flags) {
   const bool want_stream = (flags & ARIA_Q4_FLAG_KERNEL_STREAM) != 0;
   const bool want_register = (flags & ARIA_Q4_FLAG_KERNEL_REGISTER) != 0;
@@ -159,7 +167,7 @@ static int choose_kernel(int K, int N, int M, bool has_workspace, int flags) {
   if (want_register) return M <= kDecodeMaxM ? ARIA_Q4_KERNEL_REGISTER : -ARIA_Q4_EUNSUPPORTED;
   if (want_tensor) return ARIA_Q4_KERNEL_TENSOR;
   if (stream_by_default(K, N, M)) return ARIA_Q4_KERNEL_STREAM;
-  if (M <= 32 || (M <= kDecodeMaxM && !has_workspace && tc_workspace_bytes(K, N, M) > 0))
+  if (M <= 32 || (M <= kDecodeMaxM && (N <= kRegisterMaxN || (!has_workspace && tc_workspace_bytes(K, N, M) > 0))))
     return ARIA_Q4_KERNEL_REGISTER;
   return ARIA_Q4_KERNEL_TENSOR;
 }
@@ -344,6 +352,38 @@ int aria_attention_decode(const uint16_t* qkv, int M, int d, int heads, uint16_t
                                       (__half*)v_cache, (__half*)out, (cudaStream_t)stream));
 }
 
+int aria_flash_attn_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, float* lse, int NH,
+                        int T, int dh, float scale, void* stream) {
+  if (NH < 0 || T < 0 || !(scale == scale)) return ARIA_Q4_EINVAL;
+  if (dh != 64 && dh != 128) return ARIA_Q4_EUNSUPPORTED;
+  if (NH == 0 || T == 0) return ARIA_Q4_OK;
+  if (!q || !k || !v || !out) return ARIA_Q4_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return ARIA_Q4_EALIGN;
+  if ((long long)NH * ((T + 127) / 128) > 0x7fffffffLL) return ARIA_Q4_ESIZE;
+  if (int s = check_device()) return s;
+  // [NH][T][dh]: one head per "sequence" of the kernel's 4-D view
+  const long long st = (long long)T * dh;
+  return cuda_status(launch_attention_prefill((const __half*)q, (const __half*)k, (const __half*)v, dh, dh, dh, st,
+                                              NH, 1, T, scale, (__half*)out, st, 0, dh, lse, (cudaStream_t)stream));
+}
+
+int aria_attention_prefill(const uint16_t* qkv, int B, int T, int d, int heads, uint16_t* out, float* lse,
+                           void* stream) {
+  if (B < 0 || T < 0 || d <= 0 || heads <= 0 || d % heads != 0 || d % 8 != 0) return ARIA_Q4_EINVAL;
+  const int dh = d / heads;
+  if (dh != 64 && dh != 128) return ARIA_Q4_EUNSUPPORTED;
+  if (B == 0 || T == 0) return ARIA_Q4_OK;
+  if (!qkv || !out) return ARIA_Q4_EINVAL;
+  if (!aligned16(qkv) || !aligned16(out)) return ARIA_Q4_EALIGN;
+  if ((long long)B * heads * ((T + 127) / 128) > 0x7fffffffLL) return ARIA_Q4_ESIZE;
+  if (int s = check_device()) return s;
+  const __half* q = (const __half*)qkv;
+  const long long row = 3LL * d;
+  return cuda_status(launch_attention_prefill(q, q + d, q + 2 * d, dh, dh, row, row * T, B, heads, T,
+                                              1.0f / sqrtf((float)dh), (__half*)out, (long long)T * d, dh, d, lse,
+                                              (cudaStream_t)stream));
+}
+
 // ------------------------------------------------------------------ failure-path test hook
 int aria_q4_test_tensor_stall(const void* tiled, int layout, int K, int N, const uint16_t* x, int M, int ldx,
                               void* y, int y_dtype, int ldy, unsigned wait_limit_us, void* stream) {
@@ -376,7 +416,11 @@ const char* aria_q4_strerror(int status) {
 
 int aria_q4_last_cuda_error(void) { return g_last_cuda_error; }
 
-int aria_q4_take_device_error(void) { return take_device_error(); }
+int aria_q4_take_device_error(void) {
+  const int a = take_device_error();
+  const int b = attn_take_device_error();
+  return a != 0 ? a : b;
+}
 int aria_q4_abi_version(void) { return ARIA_Q4_ABI_VERSION; }
 
 }  // extern "C"

@@ -38,6 +38,9 @@
 
 namespace aria_q4 {
 
+// row tiles (16 outputs each) at or below which 16-token passes are used
+constexpr int kDecodeFewTiles = 64;
+
 struct DecodeArgs {
   const uint8_t* qs;
   const __half* scales;
@@ -401,7 +404,12 @@ cudaError_t launch_decode(const uint8_t* tiled, int layout, int K, int N, const 
   a.ksplit = S;
   a.csplit = C;
   const int gpw = (KG + S * C - 1) / (S * C);
-  const int nt = M <= 8 ? 1 : (M <= 16 ? 2 : (M <= 32 ? 4 : 8));
+  // tokens per pass (8 NT): weights with few row tiles take 16-token passes at
+  // any M (more warps in flight per SM; the weight stays in L2 between passes),
+  // the others one pass of up to 64 (measured on B200 at M = 24..64: Efkolos
+  // attn_out 2.6-2.8 us with NT = 2 against 3.6-9.0 with NT = 4 / 8, ffn_down
+  // 5.5-10.3 against 7.6-15.9; QKV, ffn_up and the LM head the other way)
+  const int nt = M <= 8 ? 1 : (M <= 16 || tiles <= kDecodeFewTiles) ? 2 : (M <= 32 ? 4 : 8);
   return layout == 1 ? launch_layout<1>(a, nt, gpw, st, pdl) : launch_layout<0>(a, nt, gpw, st, pdl);
 }
 

@@ -36,6 +36,8 @@
 // <= 2^-11 per weight); products and sums are f32 in the tensor core.
 #include <cuda.h>
 
+#include <cstring>
+
 #include "q4_common.cuh"
 #include "q4_tcgen05.cuh"
 
@@ -66,7 +68,12 @@ struct TcArgs {
   // the weights are not written by the preceding kernel on the stream: the
   // dequantisers may load and dequantise them before that kernel completes
   int const_weights;
+  // epilogue of unsplit tiles: 0 = per-thread stores (any output), else
+  // outputs staged in shared memory and written by TMA: kEpiStore (beta = 0)
+  // or kEpiAdd (beta = 1: a TMA add-reduction into y, no loads of old values)
+  int tma_epi;
 };
+enum : int { kEpiThreads = 0, kEpiStore = 1, kEpiAdd = 2 };
 
 // K-slice of work unit `unit` in 128-k groups: [g0, g1)
 __device__ __forceinline__ void tc_unit(const TcArgs& a, int unit, int KG, int& tile, int& split, int& g0, int& g1) {
@@ -86,6 +93,9 @@ constexpr int kQDepth = 4;  // 128-k code groups in flight per dequant warpgroup
 // its scales (NK: 8 B per row; KN: 256 B per 32-row group)
 constexpr int kQSlot = 128 * 64;
 constexpr int kSSlot = 128 * 8 > 4 * 256 ? 128 * 8 : 4 * 256;
+// staged epilogue: per epilogue warp, two 1-KB boxes of [16 tokens][32 rows]
+// f16 or [8 tokens][32 rows] f32
+constexpr int kEChunk = 1024;
 
 template <int BT, int STAGES>
 struct TcSmem {
@@ -93,7 +103,8 @@ struct TcSmem {
   static constexpr int kStage = 2 * kXTile;     // one 128-k stage
   static constexpr int kQOff = STAGES * kStage;
   static constexpr int kSOff = kQOff + 2 * kQDepth * kQSlot;
-  static constexpr int kBarOff = kSOff + 2 * kQDepth * kSSlot;
+  static constexpr int kEOff = kSOff + 2 * kQDepth * kSSlot;  // epilogue staging, 1024-aligned
+  static constexpr int kBarOff = kEOff + 4 * 2 * kEChunk;
   static constexpr int kBytes = kBarOff + 512 + 1024;  // barriers + alignment slack
 };
 
@@ -118,7 +129,8 @@ __device__ __forceinline__ void cp_async_wait() {
 
 template <int LAYOUT, int BT, int STAGES, int NACC>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const TcArgs a, int n_tiles, int num_tiles) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
+                   const TcArgs a, int n_tiles, int num_tiles) {
   using L = TcSmem<BT, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -188,7 +200,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc::tmem_alloc(tmem_slot, kCols);
     tc::tmem_relinquish();
   }
-  if (warp == 8 && lane == 0) tc::prefetch_tmap(&tmap_x);
+  if (warp == 8 && lane == 0) {
+    tc::prefetch_tmap(&tmap_x);
+    if (a.tma_epi != kEpiThreads) tc::prefetch_tmap(&tmap_y);
+  }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -485,7 +500,127 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool row_ok = n < a.N;
       const float bias = (a.bias && row_ok) ? __half2float(a.bias[n]) : 0.0f;
       const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT) + ((uint32_t)(q * 32) << 16);
-      if (a.splits == 1) {
+      if (a.splits == 1 && a.tma_epi != kEpiThreads) {
+        // Staged epilogue.  Per chunk of tokens the warp reads its 32 rows in
+        // the mma-fragment layout (16x256b: thread (g, t4) holds rows g, g + 8
+        // of each 16-row half, token pairs 2 t4, +1), applies alpha / bias /
+        // GELU and writes a [tokens][32 rows] box to shared memory, which lane 0
+        // hands to TMA -- a store, or for the residual term (beta = 1) an
+        // add-reduction performed at L2, so no old value is ever loaded.  f16:
+        // 16-token chunks, f16 pairs along tokens packed and transposed by
+        // stmatrix (256 outputs each), 64-byte rows with 64-byte swizzle
+        // (16-byte chunk c of row k at c ^ ((k >> 1) & 3)); f32: 8-token
+        // chunks, 128-byte rows, 128-byte swizzle.  Rows and tokens outside the
+        // tensor are clipped by TMA.
+        const int g = lane >> 2, t4 = lane & 3;
+        const int nq = (tile % n_tiles) * 128 + q * 32;
+        float bz[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int nn = nq + 8 * i + g;
+          bz[i] = (a.bias && nn < a.N) ? __half2float(a.bias[nn]) : 0.0f;
+        }
+        uint8_t* ebuf = smem + L::kEOff + q * (2 * kEChunk);
+        const bool gelu = (a.ydt & kOutGelu) != 0;
+        const bool add = a.tma_epi == kEpiAdd;
+        if (a.ydt & kOutF16) {
+          // 16-token chunks ([16 tokens][32 rows] boxes of 1 KB): two stmatrix
+          // per chunk, half the per-chunk fences and TMA issues of 8-token ones
+          // (measured: the Efkolos prefill chain at M = 4096 took 2.48 ms with
+          // 16-token and 2.96 ms with 8-token chunks)
+#pragma unroll 1
+          for (int c = 0; c < BT / 16 && m0 + c * 16 < a.M; c++) {
+            uint32_t v[2][8];
+            tc::tmem_ld_16x256b_x2(tmem_d + (uint32_t)(c * 16), v[0]);
+            tc::tmem_ld_16x256b_x2(tmem_d + (16u << 16) + (uint32_t)(c * 16), v[1]);
+            tc::tmem_ld_wait();
+            uint32_t pk[2][4];
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                // v[h][2e], v[h][2e+1]: row 16h + 8 (e & 1) + g of the warp, tokens 8 (e >> 1) + 2 t4, +1
+                const float b = bz[2 * h + (e & 1)];
+                float lo = fmaf(a.alpha, __uint_as_float(v[h][2 * e]), b);
+                float hi = fmaf(a.alpha, __uint_as_float(v[h][2 * e + 1]), b);
+                if (gelu) {
+                  lo = gelu_fast(lo);
+                  hi = gelu_fast(hi);
+                }
+                const __half2 p2 = __floats2half2_rn(lo, hi);
+                pk[h][e] = *reinterpret_cast<const uint32_t*>(&p2);
+              }
+            uint8_t* eb = ebuf + (c & 1) * kEChunk;
+            if (c >= 2) {
+              if (lane == 0) tc::bulk_wait_read<1>();  // the box written two chunks ago has been read
+              __syncwarp();
+            }
+            // matrix i = (rows 8 (i & 1) .. +7 of half h, tokens 8 (i >> 1) .. +7);
+            // lane 8i + k addresses its column k, i.e. token k + 8 (i >> 1)
+            const int mi = lane >> 3, tk = (lane & 7) + 8 * (mi >> 1);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              const int chunk = 2 * h + (mi & 1);
+              tc::stmatrix_x4_trans(tc::smem_u32(eb + tk * 64 + ((chunk ^ ((tk >> 1) & 3)) << 4)), pk[h][0],
+                                    pk[h][1], pk[h][2], pk[h][3]);
+            }
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (add)
+                tc::tma_reduce_add_2d(&tmap_y, nq, m0 + c * 16, eb);
+              else
+                tc::tma_store_2d(&tmap_y, nq, m0 + c * 16, eb);
+              tc::bulk_commit();
+            }
+          }
+        } else {
+          // f32: 16-byte chunk c of token row k at c ^ k; each value is one
+          // 4-byte shared store, conflict-free (a warp's 32 stores cover 8 rows x
+          // 4 tokens in distinct banks)
+          const int nch = min(BT / 8, (a.M - m0 + 7) / 8);
+          uint32_t v[2][4];
+          tc::tmem_ld_16x256b_x1(tmem_d, v[0]);
+          tc::tmem_ld_16x256b_x1(tmem_d + (16u << 16), v[1]);
+          tc::tmem_ld_wait_regs(v[0], v[1]);
+#pragma unroll 1
+          for (int c = 0; c < nch; c++) {
+            if (c > 0) {
+              tc::tmem_ld_16x256b_x1(tmem_d + (uint32_t)(c * 8), v[0]);
+              tc::tmem_ld_16x256b_x1(tmem_d + (16u << 16) + (uint32_t)(c * 8), v[1]);
+              tc::tmem_ld_wait_regs(v[0], v[1]);
+            }
+            uint8_t* eb = ebuf + (c & 1) * kEChunk;
+            if (c >= 2) {
+              if (lane == 0) tc::bulk_wait_read<1>();
+              __syncwarp();
+            }
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                // v[h][e]: row 16h + 8 (e >> 1) + g of the warp, token 2 t4 + (e & 1)
+                const int row = 16 * h + 8 * (e >> 1) + g, tk = 2 * t4 + (e & 1);
+                float o = fmaf(a.alpha, __uint_as_float(v[h][e]), bz[2 * h + (e >> 1)]);
+                if (gelu) o = gelu_fast(o);
+                *reinterpret_cast<float*>(eb + tk * 128 + ((((row >> 2) ^ tk) & 7) << 4) + (row & 3) * 4) = o;
+              }
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (add)
+                tc::tma_reduce_add_2d(&tmap_y, nq, m0 + c * 8, eb);
+              else
+                tc::tma_store_2d(&tmap_y, nq, m0 + c * 8, eb);
+              tc::bulk_commit();
+            }
+
+          }
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
+      } else if (a.splits == 1) {
 #pragma unroll 1
         for (int cc = 0; cc < BT / 32; cc++) {
           uint32_t v[32];
@@ -557,6 +692,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     }
+    // staged epilogue: the shared-memory boxes stay in use, and the outputs are
+    // not final, until this thread's bulk groups complete
+    if (lane == 0 && a.tma_epi != kEpiThreads) tc::bulk_wait_all();
   }
 
   tc::tc_fence_before();
@@ -620,6 +758,20 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // output boxes of the staged epilogue: [16 tokens][32 rows] f16 with 64-byte
+  // swizzle or [8 tokens][32 rows] f32 with 128-byte swizzle
+  CUtensorMap tmy;
+  memset(&tmy, 0, sizeof(tmy));
+  if (a.tma_epi != kEpiThreads) {
+    const cuuint64_t ydim[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+    const bool f16 = (a.ydt & kOutF16) != 0;
+    const cuuint64_t ystride[1] = {(cuuint64_t)a.ldy * (f16 ? 2 : 4)};
+    const cuuint32_t ybox[2] = {32u, f16 ? 16u : 8u};
+    r = enc(&tmy, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, ydim, ystride, ybox,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, f16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
   auto kern = gemm_tc_kernel<LAYOUT, BT, STAGES, NACC>;
   // the shared-memory opt-in is a per-device property of the kernel: set it once
   // on every device this instance runs on (idempotent; a racing second set is harmless)
@@ -646,7 +798,7 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, tm, a, n_tiles, num_tiles);
+  return cudaLaunchKernelEx(&cfg, kern, tm, tmy, a, n_tiles, num_tiles);
 }
 
 struct TcPlan {
@@ -681,7 +833,7 @@ static size_t tc_ws_bytes(int N, int M, int bt, int splits) {
 // on ties, i.e. when the tiles fit one round) or two (the epilogue overlapped;
 // measured on B200 at M = 4096: Efkolos LM head 255 -> 248 us, config-4
 // ffn_down 508 -> 499 us, where the model picks it).
-static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
+static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail, int epi_per_token = 8) {
   struct Cand { int bt, nacc; };
   const Cand cands[] = {{64, 2}, {128, 2}, {192, 1}, {224, 1}, {256, 1}, {192, 2}};
   const int splits_c[] = {1, 2, 3, 4, 6, 8};  // the reduction unrolls up to 8 slices
@@ -701,7 +853,7 @@ static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail) {
       const long long rounds = (units + sms - 1) / sms;
       const long long stages = (KT + S - 1) / S;
       long long cost = rounds * stages * (640 + 4 * c.bt);
-      if (c.nacc == 1) cost += (rounds - 1) * 8 * c.bt;
+      if (c.nacc == 1) cost += (rounds - 1) * (long long)epi_per_token * c.bt;
       if (S > 1) cost += rounds * (10000 + 16LL * S * c.bt);
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
@@ -745,7 +897,15 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   a.scales = reinterpret_cast<const __half*>(tiled + tiled_scale_offset(K, N));
   a.K = K; a.N = N; a.Kp = padded_k(K); a.M = M;
   a.y = y; a.ydt = ydt; a.ldy = ldy; a.bias = bias; a.alpha = alpha; a.beta = beta;
-  const TcPlan p = plan_tc(K, N, M, tc_num_sms(), workspace ? workspace_bytes : 0);
+  // outputs whose rows TMA can address (16-byte aligned base and row pitch)
+  // take the staged epilogue when the residual term is absent or beta = 1
+  const size_t esz = (ydt & kOutF16) ? 2 : 4;
+  const bool tma_ok = ((uintptr_t)y & 15u) == 0 && ((size_t)ldy * esz) % 16 == 0;
+  a.tma_epi = !tma_ok ? kEpiThreads : beta == 0.0f ? kEpiStore : beta == 1.0f ? kEpiAdd : kEpiThreads;
+  // the exposed epilogue of a single accumulator grows with GELU and the
+  // residual term's loads
+  const int epi = 8 + ((ydt & kOutGelu) ? 16 : 0) + (beta != 0.0f ? 8 : 0);
+  const TcPlan p = plan_tc(K, N, M, tc_num_sms(), workspace ? workspace_bytes : 0, epi);
   a.splits = p.splits;
   a.ws_part = nullptr;
   a.ws_cnt = nullptr;

@@ -15,7 +15,9 @@ every operation runs on the GPU through libaria_q4.so:
     logits = LayerNorm_f(h) @ embed^T                       aria_layernorm_f32 + the tied LM head (Q4_0)
 
 (above 64 sequences the LayerNorms run as aria_layernorm_f32 launches before
-the projections).
+the projections).  `prefill` runs a whole prompt per sequence at once -- the
+reference's forward_gpu -- with causal attention on the tensor cores
+(aria_attention_prefill) and fills the caches for the steps that follow.
 
 The residual stream h is f32; the LayerNorm outputs, q/k/v, the attention
 output, the FFN hidden activation and the caches are f16 (the activation type
@@ -180,6 +182,79 @@ class Decoder:
     @property
     def launches(self) -> int:
         return 1 + (5 if self.M <= 64 else 7) * self.cfg.num_layers + 2
+
+    # ------------------------------------------------------------------ prefill
+    def _prefill_buffers(self, T: int) -> dict:
+        buf = getattr(self, "_pbuf", None)
+        if buf is not None and buf["T"] == T:
+            return buf
+        cfg, n, dev = self.cfg, self.M * T, self.h.device
+        d = cfg.d_model
+        buf = {"T": T,
+               "h": torch.empty(n, d, dtype=torch.float32, device=dev),
+               "xn": torch.empty(n, d, dtype=torch.float16, device=dev),
+               "qkv": torch.empty(n, 3 * d, dtype=torch.float16, device=dev),
+               "att": torch.empty(n, d, dtype=torch.float16, device=dev),
+               "u": torch.empty(n, cfg.ffn_dim, dtype=torch.float16, device=dev),
+               "logits": torch.empty(n, cfg.vocab_size, dtype=torch.float16, device=dev),
+               "tok": torch.zeros(n, dtype=torch.int32, device=dev),
+               "pos": torch.arange(T, dtype=torch.int32, device=dev).repeat(self.M)}
+        self._pbuf = buf
+        return buf
+
+    def run_prefill(self, T: int, fill_cache: bool = True) -> torch.Tensor:
+        """The reference's whole-prompt forward (forward_gpu,
+        src/transformer_cuda.rs:1518-1873) for the M sequences of T tokens
+        already in the prefill token buffer (`prefill` fills it): embedding +
+        position, per layer LayerNorm -> QKV -> causal attention over the
+        prompt (aria_attention_prefill) -> attn_out into the f32 residual ->
+        LayerNorm -> ffn_up + GELU -> ffn_down into the residual, then the final
+        LayerNorm and the LM head over every token (f16 logits [M*T][vocab]).
+        With fill_cache, each layer's k and v rows are copied into the KV caches
+        at positions 0..T-1, so `step` continues at position T."""
+        from .attention import attention_prefill
+        cfg, w, b = self.cfg, self.w, self._prefill_buffers(T)
+        d, n = cfg.d_model, self.M * T
+        if T > w.max_seq:
+            raise ValueError(f"T={T} exceeds the cache length {w.max_seq}")
+        call("aria_embed_f16", w.embed.data_ptr(), w.pos_embed.data_ptr(), cfg.vocab_size, w.max_seq, d,
+             b["tok"].data_ptr(), b["pos"].data_ptr(), n, b["h"].data_ptr(), _stream())
+
+        def ln(g, bb):
+            call("aria_layernorm_f32", b["h"].data_ptr(), n, d, g.data_ptr(), bb.data_ptr(), LN_EPS,
+                 b["xn"].data_ptr(), d, _stream())
+
+        for i, p in enumerate(w.layers):
+            ln(p.ln1_g, p.ln1_b)
+            matmul(b["xn"], p.qkv, b["qkv"], bias=p.b_qkv, const_weights=True)
+            attention_prefill(b["qkv"], self.M, T, cfg.num_heads, out=b["att"])
+            if fill_cache:
+                qkv3 = b["qkv"].view(self.M, T, 3 * d)
+                self.k_cache[i][:, :T].copy_(qkv3[:, :, d:2 * d])
+                self.v_cache[i][:, :T].copy_(qkv3[:, :, 2 * d:])
+            matmul(b["att"], p.out, b["h"], bias=p.b_out, beta=1.0, const_weights=True)
+            ln(p.ln2_g, p.ln2_b)
+            matmul(b["xn"], p.up, b["u"], bias=p.b_up, activation="gelu", const_weights=True)
+            matmul(b["u"], p.down, b["h"], bias=p.b_down, beta=1.0, const_weights=True)
+        ln(w.lnf_g, w.lnf_b)
+        matmul(b["xn"], w.head, b["logits"], const_weights=True)
+        return b["logits"]
+
+    def prefill(self, tokens, fill_cache: bool = True) -> torch.Tensor:
+        """tokens: [M][T] ints (one prompt per sequence).  Returns the f16
+        logits [M*T][vocab] of every position (row m*T + t)."""
+        tok = torch.as_tensor(tokens, dtype=torch.int32)
+        if tok.dim() != 2 or tok.shape[0] != self.M:
+            raise ValueError(f"tokens must be [{self.M}][T]")
+        T = tok.shape[1]
+        b = self._prefill_buffers(T)
+        b["tok"].copy_(tok.reshape(-1))
+        return self.run_prefill(T, fill_cache)
+
+    def prefill_launches(self, fill_cache: bool = True) -> int:
+        """Kernels of one run_prefill (the cache copies are torch copy kernels)."""
+        per_layer = 7 + (2 if fill_cache else 0)
+        return 1 + per_layer * self.cfg.num_layers + 2
 
 
 __all__ = ["Decoder", "DecoderWeights", "sinusoidal_positions", "LN_EPS"]

@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--batched", type=lambda v: [int(t) for t in v.split(",") if t], default=[16, 64, 256])
     ap.add_argument("--scaled", type=int, default=1, help="1: also run BASELINE configs[4] (d_model 4096)")
     ap.add_argument("--scaled-prefill-tokens", type=int, default=4096)
+    ap.add_argument("--prefill-forward", type=int, default=1,
+                    help="1: also time the whole-prompt forward with causal attention (8x512, 4x2048 tokens)")
     ap.add_argument("--case", default=None,
                     help="single projection kind (qkv, attn_out, ffn_up, ffn_down, lm_head; prefix scaled_ for "
                          "BASELINE configs[4]) instead of the benchmark")
@@ -434,6 +436,65 @@ def decode_kv_section(rank, world, stream, timed, steps: int) -> dict:
     return out
 
 
+def prefill_forward_section(rank, world, stream, timed, bf16_peak: float) -> dict:
+    """The whole-prompt forward on the GPU (aria_b200.decoder.Decoder.prefill:
+    the reference's forward_gpu, src/transformer_cuda.rs:1518-1873) on the
+    Efkolos config at BASELINE configs[3]'s shapes, 8 x 512 and 4 x 2048
+    tokens: embedding, 20 x (LayerNorm, QKV, causal attention on the tensor
+    cores, attn_out, LayerNorm, ffn_up + GELU, ffn_down, KV-cache fill), final
+    LayerNorm, LM head over every token.  Also the attention kernel alone
+    (aria_attention_prefill on the step's QKV output), TFLOP/s over the causal
+    (unmasked) query-key pairs, 4 dh flops each."""
+    import torch
+    from aria_b200.attention import attention_prefill
+    from aria_b200.decoder import Decoder, DecoderWeights
+    from aria_b200.efkolos import EFKOLOS
+    cfg = EFKOLOS
+    w = DecoderWeights(cfg, max_seq=2048, seed=rank + 5)
+    out = {"workload": "Efkolos whole-prompt forward (BASELINE configs[3] token counts) with causal attention",
+           "q4_weight_bytes": w.q4_bytes}
+    dh = cfg.d_model // cfg.num_heads
+    for B, T in ((8, 512), (4, 2048)):
+        dec = Decoder(w, M=B)
+        gen = torch.Generator()
+        gen.manual_seed(rank * 7 + T)
+        tokens = torch.randint(0, cfg.vocab_size, (B, T), generator=gen)
+        dec.prefill(tokens)  # fills the token buffer, warms the path
+        with torch.cuda.stream(stream):
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                dec.run_prefill(T)
+        ms = timed(lambda i: g.replay(), 3, 3, f"aria_prefill_forward_{B}x{T}") / 3
+        del g
+        n_tok = B * T
+        attn_flops = 4 * dh * cfg.num_heads * B * T * (T + 1) // 2
+        qkv = dec._pbuf["qkv"]
+        att = dec._pbuf["att"]
+        with torch.cuda.stream(stream):
+            attention_prefill(qkv, B, T, cfg.num_heads, out=att)
+            torch.cuda.synchronize()
+            ga = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga, stream=stream):
+                for _ in range(cfg.num_layers):
+                    attention_prefill(qkv, B, T, cfg.num_heads, out=att)
+        ams = timed(lambda i: ga.replay(), 3, 2, f"aria_attention_prefill_{B}x{T}") / (3 * cfg.num_layers)
+        del ga
+        total_flops = n_tok * cfg.flops_per_token() + cfg.num_layers * attn_flops
+        out[f"{B}x{T}"] = {"ms_per_step": ms, "tokens_per_s": n_tok * world / (ms * 1e-3),
+                           "TFLOPs": total_flops * world / (ms * 1e-3) / 1e12,
+                           "launches_per_step": dec.prefill_launches(),
+                           "attention_us_per_layer": ams * 1e3,
+                           "attention_TFLOPs": attn_flops / (ams * 1e-3) / 1e12,
+                           "attention_frac_of_measured_bf16_peak": attn_flops / (ams * 1e-3) / 1e12 / bf16_peak,
+                           "attention_share_of_step": cfg.num_layers * ams / ms}
+        del dec
+        torch.cuda.empty_cache()
+    del w
+    torch.cuda.empty_cache()
+    return out
+
+
 def kernel_name(w, M: int, flags: int = 0, workspace_bytes: int = 0) -> str:
     """The kernel the library routes this projection to (aria_q4_0_kernel_choice)."""
     from aria_b200._lib import lib
@@ -757,6 +818,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         del g, pprog
         torch.cuda.empty_cache()
     decode_kv = decode_kv_section(rank, world, stream, timed, args.steps)
+    prefill_fwd = prefill_forward_section(rank, world, stream, timed, bf16_peak) if args.prefill_forward else None
     cublas = None
     if rank == 0 and world == 1 and not args.no_cublas:
         cublas = cublas_fp16_section(stream, timed, l2, ms_step,
@@ -786,6 +848,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                        "flops_per_token": flops_token, "peak_tflops_measured": bf16_peak,
                        "peak_tflops_sustained": bf16_sus, **prefill},
            "decode_step_kv": decode_kv,
+           "prefill_forward": prefill_fwd,
            "scaled": scaled,
            "gemv_config4_b1": gemv_large,
            "cublas_fp16_same_box": cublas,

@@ -251,6 +251,24 @@ ARIA_Q4_API int aria_attention_decode(const uint16_t* qkv, int M, int d, int hea
                                       uint16_t* v_cache, int max_seq, const int* positions, uint16_t* out,
                                       void* stream);
 
+/* Causal attention over whole prompts on the tensor cores: the reference's
+ * flash_attn_fwd (src/kernels.cu:1298-1437; q, k, v, out [NH][T][dh] f16,
+ * lse [NH][T] f32) with the same arguments and meaning -- out[h][t] =
+ * sum over s <= t of softmax_s(scale q[h][t].k[h][s]) v[h][s] and lse[h][t] =
+ * max + ln(sum of exp) of that row (natural log).  lse may be NULL.  dh 64 or
+ * 128; q, k, v, out 16-byte aligned.  NH = sequences x heads, T >= 1. */
+ARIA_Q4_API int aria_flash_attn_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+                                    float* lse, int NH, int T, int dh, float scale, void* stream);
+
+/* The same attention read straight from the QKV projection's output: qkv is
+ * f16 [B * T][3 d] (rows of sequence b at b T .. b T + T - 1; q, k, v of head
+ * h at columns h dh, d + h dh, 2 d + h dh), out f16 [B * T][d] with the heads
+ * side by side -- the layout attn_out reads (forward_gpu's attention block,
+ * src/transformer_cuda.rs:1583-1686).  scale 1/sqrt(dh); lse [B][heads][T] or
+ * NULL.  dh = d / heads 64 or 128; d a multiple of 8; qkv, out 16-byte aligned. */
+ARIA_Q4_API int aria_attention_prefill(const uint16_t* qkv, int B, int T, int d, int heads, uint16_t* out,
+                                       float* lse, void* stream);
+
 /* ---------------------------------------------------------------- errors */
 
 ARIA_Q4_API const char* aria_q4_strerror(int status);

@@ -80,8 +80,13 @@ def test_kernel_choice_routing():
     assert L.aria_q4_0_kernel_choice(KN, 3584, 896, 1, 0, 0) == STREAM      # tall K
     assert L.aria_q4_0_kernel_choice(KN, 896, 2688, 64, 0, 0) == TENSOR     # no K split needed
     assert L.aria_q4_0_workspace_bytes(3584, 896, 64) > 0
-    assert L.aria_q4_0_kernel_choice(NK, 3584, 896, 64, 0, 0) == REGISTER   # would split K, no workspace
-    assert L.aria_q4_0_kernel_choice(NK, 3584, 896, 64, 1 << 20, 0) == TENSOR
+    assert L.aria_q4_0_kernel_choice(NK, 3584, 896, 64, 0, 0) == REGISTER   # few row tiles (N <= 1024)
+    assert L.aria_q4_0_kernel_choice(NK, 3584, 896, 64, 1 << 20, 0) == REGISTER
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 40, 1 << 20, 0) == REGISTER
+    assert L.aria_q4_0_kernel_choice(KN, 896, 896, 65, 1 << 20, 0) == TENSOR   # above the register kernel's 64
+    assert L.aria_q4_0_workspace_bytes(16384, 4096, 64) > 0
+    assert L.aria_q4_0_kernel_choice(KN, 16384, 4096, 64, 0, 0) == REGISTER  # would split K, no workspace
+    assert L.aria_q4_0_kernel_choice(KN, 16384, 4096, 64, 64 << 20, 0) == TENSOR
     assert L.aria_q4_0_kernel_choice(KN, 896, 896, 4096, 0, 0) == TENSOR
     assert L.aria_q4_0_kernel_choice(KN, 896, 896, 1, 0, 2) == STREAM       # forced
     assert L.aria_q4_0_kernel_choice(KN, 896, 896, 9, 0, 2) == -2           # stream takes M <= 8

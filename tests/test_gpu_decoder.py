@@ -162,3 +162,32 @@ def test_decode_steps_against_oracle(coracle, cfg_kw, M, steps):
         got_v = dec.v_cache[i][:, :last].cpu().numpy().astype(np.float64)
         assert np.abs(got_k - orc.k[i][:, :last]).max() <= 2e-2
         assert np.abs(got_v - orc.v[i][:, :last]).max() <= 2e-2
+
+
+@pytest.mark.parametrize("cfg_kw,M,T", [
+    (dict(num_layers=2, d_model=256, num_heads=4, ffn_dim=1024, vocab_size=1000), 2, 40),
+    (dict(num_layers=1, d_model=896, num_heads=14, ffn_dim=3584, vocab_size=3000), 1, 130),
+])
+def test_prefill_then_decode_against_oracle(coracle, cfg_kw, M, T):
+    """Decoder.prefill (whole prompts: tensor-core projections and causal
+    attention) gives, at every position, the logits the oracle's cached step
+    gives when fed the prompt token by token; the caches it fills let `step`
+    continue at position T."""
+    from aria_b200.decoder import Decoder, DecoderWeights
+    from aria_b200.efkolos import EfkolosConfig
+    from oracle.decode_step_np import DecodeOracle
+    cfg = EfkolosConfig(**cfg_kw)
+    w = DecoderWeights(cfg, max_seq=256, seed=12)
+    dec = Decoder(w, M=M)
+    orc = DecodeOracle(coracle, _oracle_params(w), cfg, 256, M)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, cfg.vocab_size, (M, T))
+    got = dec.prefill(prompt).cpu().numpy().astype(np.float64).reshape(M, T, -1)
+    for t in range(T):
+        ref = orc.step(prompt[:, t], [t] * M)
+        if t % 13 == 0 or t == T - 1:
+            check_close(got[:, t], ref, what=f"prefill logits at position {t}")
+    for s in range(2):
+        tokens = rng.integers(0, cfg.vocab_size, M)
+        out = dec.step(tokens, [T + s] * M).cpu().numpy().astype(np.float64)
+        check_close(out, orc.step(tokens, [T + s] * M), what=f"decode step {s} after prefill")
