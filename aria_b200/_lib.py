@@ -50,6 +50,12 @@ SIGNATURES = {
     "aria_attention_decode": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _P, _P]),
     "aria_flash_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P]),
     "aria_attention_prefill": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),
+    "aria_p2p_alloc": (_I, [_SZ, _P]),
+    "aria_p2p_free": (_I, [_P]),
+    "aria_p2p_ipc_handle": (_I, [_P, _P]),
+    "aria_p2p_ipc_open": (_I, [_P, _P]),
+    "aria_p2p_ipc_close": (_I, [_P]),
+    "aria_p2p_allreduce_add": (_I, [_P, _P, _P, _I, _I, _P, _I, ctypes.c_uint, _P]),
     "aria_q4_strerror": (ctypes.c_char_p, [_I]),
     "aria_q4_last_cuda_error": (_I, []),
     "aria_q4_take_device_error": (_I, []),

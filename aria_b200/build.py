@@ -21,7 +21,7 @@ CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libaria_q4.so")
 SOURCES = ["q4_pack.cu", "q4_gemv.cu", "q4_decode.cu", "q4_gemm_tc.cu", "q4_layer.cu", "attn_prefill.cu",
-           "q4_capi.cu"]
+           "p2p_allreduce.cu", "q4_capi.cu"]
 HEADERS = ["q4_common.cuh", "q4_tcgen05.cuh"]
 
 NVCC_FLAGS = [

@@ -3,6 +3,7 @@
 // the kernels live in q4_pack.cu, q4_gemv.cu, q4_decode.cu and q4_gemm_tc.cu.
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 
 #include "../../include/aria_q4.h"
 #include "q4_common.cuh"
@@ -30,6 +31,9 @@ size_t tc_workspace_used(int K, int N, int M, size_t ws_avail);
 size_t tc_workspace_counter_bytes();
 int take_device_error();
 int attn_take_device_error();
+int p2p_take_device_error();
+cudaError_t launch_p2p_allreduce(const float* const* part, unsigned* const* flag, unsigned* state, int nranks,
+                                 int rank, __half* h, int n, unsigned long long wait_ns, cudaStream_t st);
 cudaError_t launch_attention_prefill(const __half* q, const __half* k, const __half* v, int DH, long long s_head,
                                      long long s_pos, long long s_seq, int B, int H, int T, float scale, __half* out,
                                      long long o_seq, long long o_head, long long o_pos, float* lse, cudaStream_t st);
@@ -419,7 +423,59 @@ int aria_q4_last_cuda_error(void) { return g_last_cuda_error; }
 int aria_q4_take_device_error(void) {
   const int a = take_device_error();
   const int b = attn_take_device_error();
-  return a != 0 ? a : b;
+  const int c = p2p_take_device_error();
+  return a != 0 ? a : b != 0 ? b : c;
+}
+
+// ------------------------------------------------------------------ peer reduction
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+
+int aria_p2p_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return ARIA_Q4_EINVAL;
+  if (int s = check_device()) return s;
+  void* p = nullptr;
+  if (cudaError_t e = cudaMalloc(&p, bytes)) return cuda_status(e);
+  if (cudaError_t e = cudaMemset(p, 0, bytes)) {
+    cudaFree(p);
+    return cuda_status(e);
+  }
+  *ptr = p;
+  return ARIA_Q4_OK;
+}
+
+int aria_p2p_free(void* ptr) { return ptr ? cuda_status(cudaFree(ptr)) : ARIA_Q4_OK; }
+
+int aria_p2p_ipc_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return ARIA_Q4_EINVAL;
+  cudaIpcMemHandle_t h;
+  if (cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr))) return cuda_status(e);
+  memcpy(handle, &h, sizeof(h));
+  return ARIA_Q4_OK;
+}
+
+int aria_p2p_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return ARIA_Q4_EINVAL;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int aria_p2p_ipc_close(void* ptr) { return ptr ? cuda_status(cudaIpcCloseMemHandle(ptr)) : ARIA_Q4_EINVAL; }
+
+int aria_p2p_allreduce_add(const float* const* part, unsigned* const* flag, unsigned* state, int nranks, int rank,
+                           uint16_t* h, int n, unsigned wait_limit_us, void* stream) {
+  if (nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks || n < 0 || n % 8 != 0) return ARIA_Q4_EINVAL;
+  if (wait_limit_us == 0 || wait_limit_us > 10000000u) return ARIA_Q4_EINVAL;
+  if (!part || !flag || !state || !h) return ARIA_Q4_EINVAL;
+  for (int r = 0; r < nranks; r++) {
+    if (!part[r] || !flag[r]) return ARIA_Q4_EINVAL;
+    if (!aligned16(part[r]) || ((uintptr_t)flag[r] & 3u) != 0) return ARIA_Q4_EALIGN;
+  }
+  if (!aligned16(h) || ((uintptr_t)state & 7u) != 0) return ARIA_Q4_EALIGN;
+  if (n == 0) return ARIA_Q4_OK;
+  if (int s = check_device()) return s;
+  return cuda_status(launch_p2p_allreduce(part, flag, state, nranks, rank, (__half*)h, n,
+                                          (unsigned long long)wait_limit_us * 1000ull, (cudaStream_t)stream));
 }
 int aria_q4_abi_version(void) { return ARIA_Q4_ABI_VERSION; }
 

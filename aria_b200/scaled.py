@@ -7,8 +7,10 @@ device.  Two programs:
 * `ColumnSplitDecode` -- decode at batch 64.  QKV and attn_out are replicated;
   ffn_up is column-split across the ranks (its GELU fused into the epilogue)
   and ffn_down is split along K with the same ranges, so each rank multiplies
-  the ffn_up slice it produced by its rows of ffn_down and one NCCL all-reduce
-  per layer sums the partial products into the residual stream.  The LM head is
+  the ffn_up slice it produced by its rows of ffn_down, and one reduction per
+  layer sums the partial products into the residual stream: a kernel reading
+  the peers' partials over NVLink (aria_b200.p2p, the default) or an NCCL
+  all-reduce.  The LM head is
   column-split (vocabulary rows of `embed`) and all-gathered once per step.
   Each rank quantises only its slices.
 * batch-sharded prefill -- every rank holds the full replica and runs its own
@@ -36,8 +38,15 @@ FFN_ALIGN = 128  # ffn_up column / ffn_down row ranges: whole 128-k groups of th
 
 class ColumnSplitDecode:
     def __init__(self, cfg: EfkolosConfig = SCALED, M: int = 64, world: int = 1, rank: int = 0, group=None,
-                 seed: int = 0, device="cuda"):
+                 seed: int = 0, device="cuda", reduction: str = "p2p"):
+        """reduction (world > 1): "p2p" -- one kernel per layer adds every rank's
+        ffn_down partial into the residual stream, read over NVLink from the
+        peers' memory (aria_b200.p2p); "nccl" -- NCCL all-reduce of the
+        partials, then the residual add."""
+        if reduction not in ("p2p", "nccl"):
+            raise ValueError("reduction must be 'p2p' or 'nccl'")
         self.cfg, self.M, self.world, self.rank, self.group = cfg, M, world, rank, group
+        self.reduction = reduction
         d, ff, V, L = cfg.d_model, cfg.ffn_dim, cfg.vocab_size, cfg.num_layers
         s, sd = 0.02, 0.02 / math.sqrt(2 * L)
         self.layers = []
@@ -65,24 +74,33 @@ class ColumnSplitDecode:
         self.part = torch.empty(M, d, dtype=torch.float32, device=device)
         self.logits_l = torch.empty(M, self.head_s.cols[1] - self.head_s.cols[0], dtype=torch.float16, device=device)
         self.logits = torch.empty(M, V, dtype=torch.float16, device=device)
+        self.p2p = None
+        if world > 1 and reduction == "p2p":
+            from .p2p import PeerReduction
+            self.p2p = PeerReduction(M * d, L, group)
+            self.parts = [self.p2p.part_tensor(i, (M, d)) for i in range(L)]
 
     def run(self) -> None:
         d = self.cfg.d_model
         self.h.copy_(self.h0)
-        for (qkv, out, up, dn) in self.layers:
+        for i, (qkv, out, up, dn) in enumerate(self.layers):
             matmul(self.h, qkv, self.y_qkv, const_weights=True)
             matmul(self.y_qkv[:, :d], out, self.h, beta=1.0, const_weights=True)
             if self.world == 1:
                 matmul(self.h, up, self.u, activation="gelu", const_weights=True)
                 matmul(self.u, dn, self.h, beta=1.0, const_weights=True)
                 continue
+            part = self.parts[i] if self.p2p is not None else self.part
             if up is not None:
                 matmul(self.h, up, self.u, activation="gelu", const_weights=True)
-                matmul(self.u, dn, self.part, out_dtype=torch.float32, const_weights=True)
+                matmul(self.u, dn, part, out_dtype=torch.float32, const_weights=True)
             else:
-                self.part.zero_()
-            dist.all_reduce(self.part, group=self.group)  # sum of the ranks' ffn_down partials (f32)
-            self.h.add_(self.part)  # residual add, rounded once to f16
+                part.zero_()
+            if self.p2p is not None:
+                self.p2p.reduce_into(i, self.h)  # h += every rank's partial, over peer memory
+            else:
+                dist.all_reduce(part, group=self.group)  # sum of the ranks' ffn_down partials (f32)
+                self.h.add_(part)  # residual add, rounded once to f16
         matmul(self.h, self.head, self.logits_l, const_weights=True)
         if self.world == 1:
             self.logits.copy_(self.logits_l)
@@ -97,9 +115,16 @@ class ColumnSplitDecode:
             b += q.nbytes + o.nbytes + (u.nbytes + dn.nbytes if u is not None else 0)
         return b + self.head.nbytes
 
+    def close(self) -> None:
+        """Unmaps the peers' regions and frees this rank's (p2p reduction)."""
+        if self.p2p is not None:
+            self.parts = []
+            self.p2p.close()
+            self.p2p = None
+
     def collective_bytes(self) -> int:
         """Bytes each rank contributes to the collectives per step: one f32
-        [M, d_model] all-reduce per layer and the f16 logits slice's all-gather."""
+        [M, d_model] reduction per layer and the f16 logits slice's all-gather."""
         if self.world == 1:
             return 0
         cfg = self.cfg

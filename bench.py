@@ -61,8 +61,11 @@ def parse():
                     help="1: also time the whole-prompt forward with causal attention (8x512, 4x2048 tokens)")
     ap.add_argument("--case", default=None,
                     help="single projection kind (qkv, attn_out, ffn_up, ffn_down, lm_head; prefix scaled_ for "
-                         "BASELINE configs[4]) instead of the benchmark")
-    ap.add_argument("--M", type=int, default=1, help="--case: token rows")
+                         "BASELINE configs[4]) or attention / scaled_attention, instead of the benchmark")
+    ap.add_argument("--M", type=int, default=1, help="--case: token rows (attention: positions per sequence)")
+    ap.add_argument("--seqs", type=int, default=8, help="--case attention: sequences")
+    ap.add_argument("--epilogue", default="plain", choices=["plain", "gelu", "residual", "gelu_residual"],
+                    help="--case: the projection's epilogue (GELU, residual add with beta = 1)")
     ap.add_argument("--launches", type=int, default=3, help="--case: launches before exiting")
     ap.add_argument("--kernel", default="auto", help="--case: auto, stream, register or tensor")
     ap.add_argument("--time", action="store_true", help="--case: also time the kind over weight copies")
@@ -300,16 +303,46 @@ def run_case(args) -> None:
     CUDA graph and timed with CUDA events."""
     import torch
     from aria_b200 import q4
-    from aria_b200.efkolos import synth_f16
+    from aria_b200.efkolos import EFKOLOS, SCALED, synth_f16
+    if args.case in ("attention", "scaled_attention"):
+        # causal prefill attention over the packed QKV output of --seqs
+        # sequences x --M positions (Efkolos: 14 heads x 64; scaled: 32 x 128)
+        from aria_b200.attention import attention_prefill
+        cfg = SCALED if args.case.startswith("scaled_") else EFKOLOS
+        B, T, d = args.seqs, args.M, cfg.d_model
+        qkv = synth_f16((B * T, 3 * d), 1.0, 3)
+        att = torch.empty(B * T, d, dtype=torch.float16, device="cuda")
+        for _ in range(args.launches):
+            attention_prefill(qkv, B, T, cfg.num_heads, out=att)
+        torch.cuda.synchronize()
+        out = {"case": args.case, "seqs": B, "T": T, "d": d, "heads": cfg.num_heads}
+        if args.time:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for _ in range(20):
+                    attention_prefill(qkv, B, T, cfg.num_heads, out=att)
+                e1.record(s)
+                torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1000 / 20
+            fl = 4 * (d // cfg.num_heads) * cfg.num_heads * B * T * (T + 1) // 2
+            out.update({"us_per_launch": us, "TFLOPs": fl / us / 1e6})
+        print(json.dumps(out), flush=True)
+        return
     lay, K, N, sigma = case_shape(args.case)
     shape = (K, N) if lay == q4.LAYOUT_KN else (N, K)
     w = q4.Q4Weight.from_f16(synth_f16(shape, sigma, 1), lay)
     x = synth_f16((args.M, K), 1.0, 2)
     y = torch.empty(args.M, N, dtype=torch.float16, device="cuda")
+    act = "gelu" if args.epilogue in ("gelu", "gelu_residual") else None
+    beta = 1.0 if args.epilogue in ("residual", "gelu_residual") else 0.0
     for _ in range(args.launches):
-        q4.matmul(x, w, y, kernel=args.kernel)
+        q4.matmul(x, w, y, kernel=args.kernel, activation=act, beta=beta)
     torch.cuda.synchronize()
-    out = {"case": args.case, "K": K, "N": N, "M": args.M, "kernel": kernel_name(w, args.M, flags_for(args.kernel))}
+    out = {"case": args.case, "K": K, "N": N, "M": args.M, "kernel": kernel_name(w, args.M, flags_for(args.kernel)),
+           "epilogue": args.epilogue}
     if args.time:
         l2 = torch.cuda.get_device_properties(0).L2_cache_size
         ncopy = max(4, -(-4 * l2 // w.nbytes))
@@ -346,25 +379,32 @@ def scaled_section(args, rank, world, local_rank, stream, timed, peaks):
     from aria_b200.efkolos import SCALED, DecodeProgram, Q4Stack
     from aria_b200.scaled import ColumnSplitDecode
     out = {"workload": "BASELINE configs[4]: 32 layers, d_model 4096, FFN 16384, vocab 31500"}
-    prog = ColumnSplitDecode(SCALED, M=64, world=world, rank=rank)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        prog.run()
+    for red in (("p2p", "nccl") if world > 1 else ("p2p",)):
+        prog = ColumnSplitDecode(SCALED, M=64, world=world, rank=rank, reduction=red)
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+        with torch.cuda.stream(stream):
             prog.run()
-    steps = max(5, args.steps // 10)
-    ms = timed(lambda i: g.replay(), steps, 3, "aria_scaled_decode") / steps
-    wb = prog.weight_bytes()
-    out["decode_b64_colsplit"] = {
-        "ms_per_step": ms, "tokens_per_s": 64 / (ms * 1e-3),
-        "weight_GBs_per_rank": wb / (ms * 1e-3) / 1e9, "weight_GBs_total": wb * world / (ms * 1e-3) / 1e9,
-        "collective_bytes_per_rank": prog.collective_bytes(), "collectives_per_step": prog.collectives_per_step,
-        "split": "ffn_up column-split and ffn_down split along K (one NCCL all-reduce per layer), LM head "
-                 "column-split + all-gather; QKV, attn_out replicated"}
-    del g, prog
-    torch.cuda.empty_cache()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                prog.run()
+        steps = max(5, args.steps // 10)
+        ms = timed(lambda i: g.replay(), steps, 3, f"aria_scaled_decode_{red}") / steps
+        wb = prog.weight_bytes()
+        key = "decode_b64_colsplit" if red == "p2p" else "decode_b64_colsplit_nccl"
+        out[key] = {
+            "ms_per_step": ms, "tokens_per_s": 64 / (ms * 1e-3),
+            "weight_GBs_per_rank": wb / (ms * 1e-3) / 1e9, "weight_GBs_total": wb * world / (ms * 1e-3) / 1e9,
+            "collective_bytes_per_rank": prog.collective_bytes(), "collectives_per_step": prog.collectives_per_step,
+            "split": "ffn_up column-split and ffn_down split along K, LM head column-split + NCCL all-gather; "
+                     "QKV, attn_out replicated",
+            "reduction": ("one kernel per layer reading the peers' f32 partials over NVLink and adding them into "
+                          "the residual stream" if red == "p2p" else "NCCL all-reduce + residual add per layer")
+            if world > 1 else "none (one GPU)"}
+        del g
+        prog.close()
+        del prog
+        torch.cuda.empty_cache()
     stack = Q4Stack.build(SCALED, seed=rank * 1000 + 77)
     M = args.scaled_prefill_tokens
     pprog = DecodeProgram(stack, M=M, seed=rank + 31)

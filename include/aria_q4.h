@@ -269,6 +269,42 @@ ARIA_Q4_API int aria_flash_attn_fwd(const uint16_t* q, const uint16_t* k, const 
 ARIA_Q4_API int aria_attention_prefill(const uint16_t* qkv, int B, int T, int d, int heads, uint16_t* out,
                                        float* lse, void* stream);
 
+/* ---------------------------------------------------------------- multi-GPU */
+
+/* The reduction of the column-split FFN over NVLink peer memory (BASELINE
+ * configs[4] decode on 2..8 GPUs of one node): replaces an NCCL all-reduce of
+ * the ranks' f32 ffn_down partials followed by the residual add.  No
+ * reference counterpart (the reference runs on one device,
+ * src/transformer_cuda.rs:83-103).
+ *
+ * Set-up (once, outside any stream capture): every rank allocates one region
+ * with aria_p2p_alloc (zero-filled; the only allocating call of the library),
+ * exports it with aria_p2p_ipc_handle, exchanges the 64-byte handles with its
+ * peers (any host channel) and maps theirs with aria_p2p_ipc_open.  Each
+ * region holds, at offsets the caller chooses, one f32 partial buffer per
+ * layer, a flag block of 8 unsigned words and a state block of 2 words.
+ *
+ * aria_p2p_allreduce_add: h[0..n) (f16) += sum over ranks r of part[r][0..n)
+ * (f32, rank order, identical bits on every rank), where part[r] is this
+ * layer's partial buffer on rank r (the peers' through their mappings) and
+ * flag[r] rank r's flag block; state is this rank's state block.  Every rank
+ * must make the same sequence of calls (a call per layer, layers in order);
+ * the partial of a layer must not be rewritten before the following call has
+ * completed on this rank (one buffer per layer satisfies it).  The call
+ * waits on the GPU (bounded by wait_limit_us, 1..10^7) for every peer's
+ * partial of the same call; if one never arrives it records
+ * ARIA_Q4_DEVERR_PEER_TIMEOUT, leaves h unchanged and returns.  nranks 1..8,
+ * n a multiple of 8, h and the partials 16-byte aligned.  part and flag are
+ * HOST arrays of nranks device pointers.  Stream-ordered; captured launches
+ * stay correct on replay (the call counter lives in the state block). */
+ARIA_Q4_API int aria_p2p_alloc(size_t bytes, void** ptr);
+ARIA_Q4_API int aria_p2p_free(void* ptr);
+ARIA_Q4_API int aria_p2p_ipc_handle(const void* ptr, void* handle /* 64 bytes */);
+ARIA_Q4_API int aria_p2p_ipc_open(const void* handle /* 64 bytes */, void** ptr);
+ARIA_Q4_API int aria_p2p_ipc_close(void* ptr);
+ARIA_Q4_API int aria_p2p_allreduce_add(const float* const* part, unsigned* const* flag, unsigned* state, int nranks,
+                                       int rank, uint16_t* h, int n, unsigned wait_limit_us, void* stream);
+
 /* ---------------------------------------------------------------- errors */
 
 ARIA_Q4_API const char* aria_q4_strerror(int status);
@@ -279,13 +315,15 @@ enum {
   ARIA_Q4_DEVERR_NONE = 0,
   ARIA_Q4_DEVERR_TIMEOUT_FULL = 1,   /* the MMA issuer waited too long for an operand stage */
   ARIA_Q4_DEVERR_TIMEOUT_EMPTY = 2,  /* a producer waited too long for a free stage */
-  ARIA_Q4_DEVERR_TIMEOUT_ACCUM = 3   /* an accumulator hand-off waited too long */
+  ARIA_Q4_DEVERR_TIMEOUT_ACCUM = 3,  /* an accumulator hand-off waited too long */
+  ARIA_Q4_DEVERR_PEER_TIMEOUT = 4    /* aria_p2p_allreduce_add: a peer never published its partial */
 };
 
 /* Reads and clears the device-side error code of the current device: 0 = none,
- * ARIA_Q4_DEVERR_* = a bounded wait inside the tcgen05 kernel expired (the
- * kernel recorded the first such wait, unwound and returned without finishing
- * its tiles instead of hanging), -1 = the read failed.  One code per device,
+ * ARIA_Q4_DEVERR_* = a bounded wait inside a kernel expired (the tcgen05
+ * kernels record the first such wait, unwind and return without finishing
+ * their tiles instead of hanging; the peer reduction leaves h unchanged),
+ * -1 = the read failed.  One code per device,
  * shared by every stream and thread.  Synchronises the device.  No reference
  * counterpart (the reference aborts). */
 ARIA_Q4_API int aria_q4_take_device_error(void);

@@ -155,3 +155,29 @@ def test_ffn_pair_split_allreduce_gloo(world, d, ff, M):
     for rank, same, err in res:
         assert same, f"rank {rank}: ffn_up columns and ffn_down rows differ"
         assert err < 1e-9, f"rank {rank}: all-reduced pair off by {err}"
+
+
+def _handles_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from aria_b200.p2p import exchange_handles
+    got = exchange_handles(bytes([rank]) * 64)
+    dist.destroy_process_group()
+    q.put((rank, got))
+
+
+def test_ipc_handle_exchange_gloo():
+    """aria_b200.p2p.exchange_handles: every rank receives every 64-byte handle in rank order."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 200
+    procs = [ctx.Process(target=_handles_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, got in res:
+        assert got == [bytes([r]) * 64 for r in range(3)]

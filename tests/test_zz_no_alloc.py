@@ -49,10 +49,11 @@ def _setup(q4, coracle, layout, K, N, M):
 
 
 @pytest.mark.parametrize("layout,K,N,M,splits", [
-    (LAYOUT_KN, 16384, 512, 64, True),   # K split over the scratch
-    (LAYOUT_NK, 3584, 896, 64, True),
-    (LAYOUT_KN, 8224, 256, 50, True),
+    (LAYOUT_KN, 16384, 1536, 64, True),  # K split over the scratch
+    (LAYOUT_NK, 3584, 1536, 64, True),
+    (LAYOUT_KN, 8224, 1280, 50, True),
     (LAYOUT_KN, 896, 2688, 64, False),   # no split: no scratch used
+    (LAYOUT_NK, 3584, 896, 64, False),   # register-fed kernel (few row tiles): no scratch
     (LAYOUT_NK, 4096, 1001, 1, False),
 ])
 def test_static_scratch_matches_caller_workspace(q4, coracle, layout, K, N, M, splits):
@@ -63,8 +64,8 @@ def test_static_scratch_matches_caller_workspace(q4, coracle, layout, K, N, M, s
         # the planner splits K for this shape, within the static scratch
         assert 0 < need <= STATIC_BYTES
         assert lib.aria_q4_0_kernel_choice(layout, K, N, M, STATIC_BYTES, 0) == TENSOR
-    else:
-        assert need == 0
+    else:  # no split, or a kernel other than the tensor-core one (which alone uses scratch)
+        assert need == 0 or lib.aria_q4_0_kernel_choice(layout, K, N, M, STATIC_BYTES, 0) != TENSOR
     blocks, wq, x, bias, xh, bh = _setup(q4, coracle, layout, K, N, M)
     ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
     outs = []
