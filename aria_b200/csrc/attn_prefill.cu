@@ -8,8 +8,9 @@
 // same outputs -- out = softmax(scale q k^T, causal) v and lse = max + ln(sum)
 // per query row -- with the products on the tensor cores:
 //
-// One CTA per (sequence, head, 128-query tile), heaviest tiles first.  For
-// every 128-key block j up to the diagonal:
+// Persistent: one CTA per SM walks the (sequence, head, 128-query tile) work
+// items, heaviest tiles first, round-robin.  For every 128-key block j of a
+// tile, up to the diagonal:
 //   S_j = Q K_j^T     tcgen05.mma, A = Q tile and B = K block from shared memory
 //                     (TMA, 128-byte swizzle), f32 S in tensor memory (128 x 128)
 //   P_j = exp2(S_j - m) per row, written as f16 over S_j's own TMEM columns
@@ -68,11 +69,26 @@ struct AttnSmem {
   static constexpr int kVOff = kKOff + 2 * kKV;          // V block (one: the transposers turn it over fast)
   static constexpr int kVtOff = kVOff + kKV;             // [2] V^T stages: 2 boxes of [DH rows][128 B]
   static constexpr int kRedOff = kVtOff + 2 * kKV;       // row-max exchange [2 parity][2 halves][128] f32
-  static constexpr int kBarOff = kRedOff + 2 * 2 * kBQ * 4;
+  static constexpr int kSumOff = kRedOff + 2 * 2 * kBQ * 4;  // row-sum exchange [2 halves][128] f32
+  static constexpr int kBarOff = kSumOff + 2 * kBQ * 4;
   static constexpr int kBytes = kBarOff + 256 + 1024;
 };
 
-__device__ __forceinline__ float rl_sum(const float* rl, int r) { return rl[r] + rl[kBQ + r]; }
+// Query tile t of the persistent schedule: heaviest (last) tiles first.
+struct AttnTile {
+  int seq, head, q0, nb;
+};
+__device__ __forceinline__ AttnTile attn_tile(const AttnArgs& a, int t) {
+  const int bh_count = a.B * a.H;
+  const int qt = a.n_qt - 1 - t / bh_count;
+  const int bh = t % bh_count;
+  AttnTile r;
+  r.seq = bh / a.H;
+  r.head = bh % a.H;
+  r.q0 = qt * kBQ;
+  r.nb = min(qt + 1, (a.T + kBK - 1) / kBK);  // key blocks up to the diagonal
+  return r;
+}
 
 template <int DH>
 __global__ void __maxnreg__(168)
@@ -82,7 +98,8 @@ __global__ void __maxnreg__(168)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* k_full = q_full + 1;     // [2]
+  uint64_t* q_empty = q_full + 1;    // S MMA commit after a tile's last block
+  uint64_t* k_full = q_empty + 1;    // [2]
   uint64_t* k_empty = k_full + 2;    // [2] S MMA commit
   uint64_t* v_full = k_empty + 2;    // [1]
   uint64_t* v_empty = v_full + 1;    // [1] 2 transposer warps
@@ -98,22 +115,18 @@ __global__ void __maxnreg__(168)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + L::kRedOff);
+  float* rsum = reinterpret_cast<float*>(smem + L::kSumOff);
   auto give_up = [&](int wait_result, int code) {
     if (wait_result == tc::kWaitTimeout) tc::record_error(code);
     atomicExch(abort_flag, 1);
   };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // heaviest (last) query tiles first
-  const int bh_count = a.B * a.H;
-  const int qt = a.n_qt - 1 - (int)blockIdx.x / bh_count;
-  const int bh = (int)blockIdx.x % bh_count;
-  const int seq = bh / a.H, head = bh % a.H;
-  const int q0 = qt * kBQ;
-  const int nb = min(qt + 1, (a.T + kBK - 1) / kBK);  // key blocks up to the diagonal
+  const int n_tiles = a.n_qt * a.B * a.H;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
+    tc::mbar_init(q_empty, 1);
     for (int s = 0; s < 2; s++) {
       tc::mbar_init(&k_full[s], 1);
       tc::mbar_init(&k_empty[s], 1);
@@ -151,50 +164,52 @@ __global__ void __maxnreg__(168)
   grid_dep_launch();
   grid_dep_wait();  // q, k, v are the preceding kernel's outputs
 
+  // Every role walks the same tiles (t = blockIdx.x, + gridDim.x, ...) and the
+  // same key blocks; barrier phases follow the CTA-wide block counter g (and
+  // the tile counter it for the Q buffer).
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int issued = 0;
+      int g = 0, it = 0;
+      int gk = 0, gv = 0;  // K and V blocks whose copies were issued
       bool ok = true;
-      tc::mbar_arrive_expect_tx(q_full, L::kQ);
-#pragma unroll
-      for (int c = 0; c < DH / 64; c++)
-        tc::tma_load_4d(smem + L::kQOff + c * (kBQ * 128), &tm_q, 64 * c, head, q0, seq, q_full);
-      int issued_v = 0;
-      for (int j = 0; j < nb && ok; j++) {
-        const int s = j & 1;
-        if (j >= 2) {
-          const int w = tc::mbar_wait_or_abort(&k_empty[s], ((j >> 1) - 1) & 1, 2 * a.wait_ns, abort_flag);
-          if (w != tc::kWaitOk) {
-            give_up(w, tc::kErrTimeoutEmpty);
-            ok = false;
-            break;
-          }
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        const int w = tc::mbar_wait_or_abort(bar, parity, 2 * a.wait_ns, abort_flag);
+        if (w != tc::kWaitOk) {
+          give_up(w, tc::kErrTimeoutEmpty);
+          ok = false;
         }
-        tc::mbar_arrive_expect_tx(&k_full[s], L::kKV);
+        return ok;
+      };
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, it++) {
+        const AttnTile tl = attn_tile(a, t);
+        if (it >= 1 && !wait(q_empty, (it - 1) & 1)) break;
+        tc::mbar_arrive_expect_tx(q_full, L::kQ);
 #pragma unroll
         for (int c = 0; c < DH / 64; c++)
-          tc::tma_load_4d(smem + L::kKOff + s * L::kKV + c * (kBK * 128), &tm_k, 64 * c, head, j * kBK, seq,
-                          &k_full[s]);
-        issued = j + 1;
-        if (j >= 1) {
-          const int w = tc::mbar_wait_or_abort(v_empty, (j - 1) & 1, 2 * a.wait_ns, abort_flag);
-          if (w != tc::kWaitOk) {
-            give_up(w, tc::kErrTimeoutEmpty);
-            ok = false;
-            break;
-          }
-        }
-        tc::mbar_arrive_expect_tx(v_full, L::kKV);
+          tc::tma_load_4d(smem + L::kQOff + c * (kBQ * 128), &tm_q, 64 * c, tl.head, tl.q0, tl.seq, q_full);
+        for (int j = 0; j < tl.nb; j++, g++) {
+          const int s = g & 1;
+          if (g >= 2 && !wait(&k_empty[s], ((g >> 1) - 1) & 1)) break;
+          tc::mbar_arrive_expect_tx(&k_full[s], L::kKV);
 #pragma unroll
-        for (int c = 0; c < DH / 64; c++)
-          tc::tma_load_4d(smem + L::kVOff + c * (kBK * 128), &tm_v, 64 * c, head, j * kBK, seq, v_full);
-        issued_v = j + 1;
+          for (int c = 0; c < DH / 64; c++)
+            tc::tma_load_4d(smem + L::kKOff + s * L::kKV + c * (kBK * 128), &tm_k, 64 * c, tl.head, j * kBK, tl.seq,
+                            &k_full[s]);
+          gk = g + 1;
+          if (g >= 1 && !wait(v_empty, (g - 1) & 1)) break;
+          tc::mbar_arrive_expect_tx(v_full, L::kKV);
+#pragma unroll
+          for (int c = 0; c < DH / 64; c++)
+            tc::tma_load_4d(smem + L::kVOff + c * (kBK * 128), &tm_v, 64 * c, tl.head, j * kBK, tl.seq, v_full);
+          gv = g + 1;
+        }
       }
-      // no copy into shared memory may be in flight when the CTA exits
-      tc::mbar_wait(q_full, 0);
-      for (int j = (issued > 2 ? issued - 2 : 0); j < issued; j++) tc::mbar_wait(&k_full[j & 1], (j >> 1) & 1);
-      if (issued_v > 0) tc::mbar_wait(v_full, (issued_v - 1) & 1);
+      // no copy into shared memory may be in flight when the CTA exits: the
+      // last Q tile, the last two K blocks and the last V block issued
+      if (it >= 1) tc::mbar_wait(q_full, (it - 1) & 1);
+      for (int i = (gk > 2 ? gk - 2 : 0); i < gk; i++) tc::mbar_wait(&k_full[i & 1], (i >> 1) & 1);
+      if (gv >= 1) tc::mbar_wait(v_full, (gv - 1) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -212,11 +227,11 @@ __global__ void __maxnreg__(168)
         }
         return ok;
       };
-      auto issue_o = [&](int i) {
-        const int b = i & 1;
-        if (!wait(&p_full[b], (i >> 1) & 1, tc::kErrTimeoutFull)) return;
-        if (!wait(&vt_full[b], (i >> 1) & 1, tc::kErrTimeoutFull)) return;
-        if (i >= 2 && !wait(&o_empty[b], ((i >> 1) - 1) & 1, tc::kErrTimeoutAccum)) return;
+      auto issue_o = [&](int gi) {
+        const int b = gi & 1;
+        if (!wait(&p_full[b], (gi >> 1) & 1, tc::kErrTimeoutFull)) return;
+        if (!wait(&vt_full[b], (gi >> 1) & 1, tc::kErrTimeoutFull)) return;
+        if (gi >= 2 && !wait(&o_empty[b], ((gi >> 1) - 1) & 1, tc::kErrTimeoutAccum)) return;
         tc::tc_fence_after();
         const uint32_t vt = tc::smem_u32(smem + L::kVtOff + b * L::kKV);
 #pragma unroll
@@ -228,11 +243,14 @@ __global__ void __maxnreg__(168)
         tc::umma_commit(&s_empty[b]);
         tc::umma_commit(&vt_empty[b]);
       };
-      if (wait(q_full, 0, tc::kErrTimeoutFull)) {
-        for (int j = 0; j < nb && ok; j++) {
-          const int b = j & 1;
-          if (!wait(&k_full[b], (j >> 1) & 1, tc::kErrTimeoutFull)) break;
-          if (j >= 2 && !wait(&s_empty[b], ((j >> 1) - 1) & 1, tc::kErrTimeoutAccum)) break;
+      int g = 0, it = 0;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, it++) {
+        const AttnTile tl = attn_tile(a, t);
+        if (!wait(q_full, it & 1, tc::kErrTimeoutFull)) break;
+        for (int j = 0; j < tl.nb && ok; j++, g++) {
+          const int b = g & 1;
+          if (!wait(&k_full[b], (g >> 1) & 1, tc::kErrTimeoutFull)) break;
+          if (g >= 2 && !wait(&s_empty[b], ((g >> 1) - 1) & 1, tc::kErrTimeoutAccum)) break;
           tc::tc_fence_after();
           const uint32_t ks = tc::smem_u32(smem + L::kKOff + b * L::kKV);
 #pragma unroll
@@ -242,9 +260,10 @@ __global__ void __maxnreg__(168)
                          tc::sdesc_k_sw128(ks + (kk >> 2) * (kBK * 128) + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
           tc::umma_commit(&s_full[b]);
           tc::umma_commit(&k_empty[b]);
-          if (j >= 1) issue_o(j - 1);
+          if (j == tl.nb - 1) tc::umma_commit(q_empty);  // the tile's last product with Q
+          if (j >= 1) issue_o(g - 1);
         }
-        if (ok) issue_o(nb - 1);
+        if (ok) issue_o(g - 1);
       }
       if (!ok) {
         // no MMA of this thread may still write tensor memory when it is freed
@@ -257,14 +276,8 @@ __global__ void __maxnreg__(168)
     const int qd = warp & 3;            // TMEM lane quadrant
     const int hf = (warp - 2) >> 2;     // half of the keys / of the output columns
     const int r = qd * 32 + lane;       // query row of the tile = TMEM lane
-    const int qi = q0 + r;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
     constexpr int OC = DH / 2;          // output columns of this thread
-    float o[OC];
-#pragma unroll
-    for (int c = 0; c < OC; c++) o[c] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
-    float alpha_prev = 0.0f;
     bool ok = true;
     int pair_uses = 0;
     auto wait = [&](uint64_t* bar, uint32_t parity, int code) {
@@ -288,93 +301,106 @@ __global__ void __maxnreg__(168)
       tc::tc_fence_after();
       return met;
     };
-    auto accumulate = [&](int i, float alpha) {
-      const int b = i & 1;
-      if (!wait(&o_full[b], (i >> 1) & 1, tc::kErrTimeoutAccum)) return;
+    float o[OC];
+    auto accumulate = [&](int gi, float alpha) {
+      const int b = gi & 1;
+      if (!wait(&o_full[b], (gi >> 1) & 1, tc::kErrTimeoutAccum)) return;
       tc::tc_fence_after();
 #pragma unroll
-      for (int c0 = 0; c0 < OC; c0 += 16) {
-        uint32_t v[16];
-        tc::tmem_ld_32x32b_x16(tmem_base + lane_off + kOCol + (uint32_t)(b * DH + hf * OC + c0), v);
+      for (int c0 = 0; c0 < OC; c0 += 32) {
+        uint32_t v[32];
+        tc::tmem_ld_32x32b_x16(tmem_base + lane_off + kOCol + (uint32_t)(b * DH + hf * OC + c0),
+                               *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+        tc::tmem_ld_32x32b_x16(tmem_base + lane_off + kOCol + (uint32_t)(b * DH + hf * OC + c0 + 16),
+                               *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 16; c++) o[c0 + c] = fmaf(o[c0 + c], alpha, __uint_as_float(v[c]));
+        for (int c = 0; c < 32; c++) o[c0 + c] = fmaf(o[c0 + c], alpha, __uint_as_float(v[c]));
       }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&o_empty[b]);
     };
-    for (int j = 0; j < nb && ok; j++) {
-      const int b = j & 1;
-      if (!wait(&s_full[b], (j >> 1) & 1, tc::kErrTimeoutFull)) break;
-      tc::tc_fence_after();
-      // pass 1: this half's 64 scores (scaled, log2 domain; keys after the query
-      // or past the sequence are -inf) -> row maximum
-      const int k0 = j * kBK + hf * 64;
-      const int kmax = min(qi, a.T - 1) - k0;  // keys e <= kmax are visible
-      const uint32_t scol = tmem_base + lane_off + (uint32_t)(b * 128 + hf * 64);
-      float mx = -INFINITY;
+    int g = 0;
+    for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+      const AttnTile tl = attn_tile(a, t);
+      const int qi = tl.q0 + r;
 #pragma unroll
-      for (int c = 0; c < 2; c++) {
-        uint32_t sv[32];
-        tc::tmem_ld_32x32b_x32(scol + (uint32_t)(32 * c), sv);
-        tc::tmem_ld_wait();
+      for (int c = 0; c < OC; c++) o[c] = 0.0f;
+      float m = -INFINITY, l = 0.0f;
+      float alpha_prev = 0.0f;
+      for (int j = 0; j < tl.nb && ok; j++, g++) {
+        const int b = g & 1;
+        if (!wait(&s_full[b], (g >> 1) & 1, tc::kErrTimeoutFull)) break;
+        tc::tc_fence_after();
+        // pass 1: this half's 64 scores (scaled, log2 domain; keys after the
+        // query or past the sequence are -inf) -> row maximum
+        const int kmax = min(qi, a.T - 1) - (j * kBK + hf * 64);  // keys e <= kmax are visible
+        const uint32_t scol = tmem_base + lane_off + (uint32_t)(b * 128 + hf * 64);
+        float mx = -INFINITY;
+        {
+          uint32_t sv[64];
+          tc::tmem_ld_32x32b_x32(scol, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tc::tmem_ld_32x32b_x32(scol + 32u, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tc::tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; e++)
-          if (32 * c + e <= kmax) mx = fmaxf(mx, __uint_as_float(sv[e]) * a.scale_log2);
-      }
-      float* rd = red + (j & 1) * (2 * kBQ);
-      rd[hf * kBQ + r] = mx;
-      if (!pair_sync()) break;  // both warps of this quadrant have written their maxima
-      mx = fmaxf(rd[r], rd[kBQ + r]);
-      const float m_new = fmaxf(m, mx);
-      // a row with no visible key so far keeps m = -inf; its alpha is 1 and p 0
-      const float alpha = m_new == -INFINITY ? 1.0f : tc::ex2_approx(m - m_new);
-      const float msub = m_new == -INFINITY ? 0.0f : m_new;
-      m = m_new;
-      // pass 2: p = exp2(s - m) as f16 pairs along keys, written over this half's
-      // own S columns (keys hf*64 + 16u .. +15 -> columns hf*64 + 8u .. +7), which
-      // it has read already; the O product addresses its A slices there.  Chunks
-      // of 16 columns keep the registers for the output row (dh / 2 per thread).
-      float sum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        uint32_t sv[16];
-        tc::tmem_ld_32x32b_x16(scol + (uint32_t)(16 * c), sv);
-        tc::tmem_ld_wait();
-        uint32_t pk[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const float x0 = 16 * c + 2 * e <= kmax ? __uint_as_float(sv[2 * e]) * a.scale_log2 : -INFINITY;
-          const float x1 = 16 * c + 2 * e + 1 <= kmax ? __uint_as_float(sv[2 * e + 1]) * a.scale_log2 : -INFINITY;
-          const float p0 = tc::ex2_approx(x0 - msub);
-          const float p1 = tc::ex2_approx(x1 - msub);
-          sum += p0 + p1;
-          const __half2 h2 = __floats2half2_rn(p0, p1);
-          pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+          for (int e = 0; e < 64; e++)
+            if (e <= kmax) mx = fmaxf(mx, __uint_as_float(sv[e]));
         }
-        tc::tmem_st_32x32b_x8(scol + (uint32_t)(8 * c), pk);
+        mx *= a.scale_log2;  // scale > 0: the maximum commutes with it
+        float* rd = red + (g & 1) * (2 * kBQ);
+        rd[hf * kBQ + r] = mx;
+        if (!pair_sync()) break;  // both warps of this quadrant have written their maxima
+        mx = fmaxf(rd[r], rd[kBQ + r]);
+        const float m_new = fmaxf(m, mx);
+        // a row with no visible key so far keeps m = -inf; its alpha is 1 and p 0
+        const float alpha = m_new == -INFINITY ? 1.0f : tc::ex2_approx(m - m_new);
+        const float msub = m_new == -INFINITY ? 0.0f : m_new;
+        m = m_new;
+        // pass 2: p = exp2(s - m) as f16 pairs along keys, written over this
+        // half's own S columns (keys hf*64 + 16u .. +15 -> columns hf*64 + 8u ..
+        // +7), which it has read already; the O product addresses its A slices
+        // there.  32 scores per TMEM wait.
+        float sum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+          uint32_t sv[32];
+          tc::tmem_ld_32x32b_x16(scol + (uint32_t)(32 * c), *reinterpret_cast<uint32_t(*)[16]>(&sv[0]));
+          tc::tmem_ld_32x32b_x16(scol + (uint32_t)(32 * c + 16), *reinterpret_cast<uint32_t(*)[16]>(&sv[16]));
+          tc::tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; e++) {
+            const int k = 32 * c + 2 * e;
+            const float x0 = k <= kmax ? fmaf(__uint_as_float(sv[2 * e]), a.scale_log2, -msub) : -INFINITY;
+            const float x1 = k + 1 <= kmax ? fmaf(__uint_as_float(sv[2 * e + 1]), a.scale_log2, -msub) : -INFINITY;
+            const float p0 = tc::ex2_approx(x0);
+            const float p1 = tc::ex2_approx(x1);
+            sum += p0 + p1;
+            const __half2 h2 = __floats2half2_rn(p0, p1);
+            pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          tc::tmem_st_32x32b_x16(scol + (uint32_t)(16 * c), pk);
+        }
+        tc::tmem_st_wait();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&p_full[b]);
+        l = fmaf(l, alpha, sum);
+        if (j >= 1) accumulate(g - 1, alpha_prev);
+        alpha_prev = alpha;
       }
-      tc::tmem_st_wait();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&p_full[b]);
-      l = fmaf(l, alpha, sum);
-      if (j >= 1) accumulate(j - 1, alpha_prev);
-      alpha_prev = alpha;
-    }
-    if (ok) accumulate(nb - 1, alpha_prev);
-    if (ok) {
+      if (!ok) break;
+      accumulate(g - 1, alpha_prev);
+      if (!ok) break;
       // the row's sum is the two halves' sums (same running maximum)
-      float* rl = red + (nb & 1) * (2 * kBQ);  // the parity buffer the last exchange did not use
-      rl[hf * kBQ + r] = l;
-      ok = pair_sync();
-    }
-    if (ok) {
-      const float lt = rl_sum(red + (nb & 1) * (2 * kBQ), r);
+      rsum[hf * kBQ + r] = l;
+      if (!pair_sync()) break;
+      const float lt = rsum[r] + rsum[kBQ + r];
       const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
       if (qi < a.T) {
-        __half* op = a.out + (long long)seq * a.o_seq + (long long)head * a.o_head + (long long)qi * a.o_pos + hf * OC;
+        __half* op =
+            a.out + (long long)tl.seq * a.o_seq + (long long)tl.head * a.o_head + (long long)qi * a.o_pos + hf * OC;
 #pragma unroll
         for (int c = 0; c < OC; c += 8) {
           uint4 w;
@@ -389,7 +415,8 @@ __global__ void __maxnreg__(168)
           *reinterpret_cast<uint4*>(op + c) = w;
         }
         if (a.lse && hf == 0)
-          a.lse[((long long)seq * a.H + head) * a.T + qi] = (m + __log2f(lt > 0.0f ? lt : 1e-30f)) * 0.69314718f;
+          a.lse[((long long)tl.seq * a.H + tl.head) * a.T + qi] =
+              (m + __log2f(lt > 0.0f ? lt : 1e-30f)) * 0.69314718f;
       }
     }
   } else {
@@ -400,39 +427,47 @@ __global__ void __maxnreg__(168)
     // block i; a warp takes blocks (key group kb, column group cb) in turn.
     const int tw = warp - 10;
     constexpr int kBlocks = (kBK / 8) * (DH / 8);
-    for (int j = 0; j < nb; j++) {
-      const int s = j & 1;
-      int w = tc::mbar_wait_or_abort(v_full, j & 1, 2 * a.wait_ns, abort_flag);
-      if (w == tc::kWaitOk && j >= 2) w = tc::mbar_wait_or_abort(&vt_empty[s], ((j >> 1) - 1) & 1, 2 * a.wait_ns, abort_flag);
-      const bool all_ok = __all_sync(0xffffffffu, w == tc::kWaitOk);
-      if (!all_ok) {
-        if (lane == 0) give_up(__any_sync(0xffffffffu, w == tc::kWaitTimeout) ? tc::kWaitTimeout : tc::kWaitAborted,
-                               tc::kErrTimeoutEmpty);
-        break;
-      }
-      const uint8_t* vsrc = smem + L::kVOff;
-      uint8_t* vdst = smem + L::kVtOff + s * L::kKV;
-      const int mi = lane >> 3, k8 = lane & 7;
-      for (int blk = tw * 4; blk < kBlocks; blk += 8) {
-        // four blocks blk .. blk + 3: key group kb, column groups cb .. cb + 3
-        const int kb = blk / (DH / 8), cb = (blk % (DH / 8)) + mi;
-        const int key = kb * 8 + k8, col = cb * 8;
-        const uint32_t src = tc::smem_u32(vsrc + (col >> 6) * (kBK * 128) + key * 128 +
-                                          ((((col & 63) >> 3) ^ (key & 7)) << 4));
-        uint32_t r0, r1, r2, r3;
-        tc::ldmatrix_x4_trans(src, r0, r1, r2, r3);
-        // r[i] now holds the fragment of block i's transpose (rows = columns of V)
-        const int vrow = cb * 8 + k8;  // lane 8i + k8 stores row k8 of transposed block i
-        const int kk = kb * 8;         // its 8 keys
-        const uint32_t dst = tc::smem_u32(vdst + (kk >> 6) * (DH * 128) + vrow * 128 +
-                                          ((((kk & 63) >> 3) ^ (vrow & 7)) << 4));
-        tc::stmatrix_x4(dst, r0, r1, r2, r3);
-      }
-      tc::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tc::mbar_arrive(&vt_full[s]);
-        tc::mbar_arrive(v_empty);
+    int g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+      const AttnTile tl = attn_tile(a, t);
+      for (int j = 0; j < tl.nb; j++, g++) {
+        const int s = g & 1;
+        int w = tc::mbar_wait_or_abort(v_full, g & 1, 2 * a.wait_ns, abort_flag);
+        if (w == tc::kWaitOk && g >= 2)
+          w = tc::mbar_wait_or_abort(&vt_empty[s], ((g >> 1) - 1) & 1, 2 * a.wait_ns, abort_flag);
+        const bool all_ok = __all_sync(0xffffffffu, w == tc::kWaitOk);
+        if (!all_ok) {
+          if (lane == 0)
+            give_up(__any_sync(0xffffffffu, w == tc::kWaitTimeout) ? tc::kWaitTimeout : tc::kWaitAborted,
+                    tc::kErrTimeoutEmpty);
+          ok = false;
+          break;
+        }
+        const uint8_t* vsrc = smem + L::kVOff;
+        uint8_t* vdst = smem + L::kVtOff + s * L::kKV;
+        const int mi = lane >> 3, k8 = lane & 7;
+        for (int blk = tw * 4; blk < kBlocks; blk += 8) {
+          // four blocks blk .. blk + 3: key group kb, column groups cb .. cb + 3
+          const int kb = blk / (DH / 8), cb = (blk % (DH / 8)) + mi;
+          const int key = kb * 8 + k8, col = cb * 8;
+          const uint32_t src = tc::smem_u32(vsrc + (col >> 6) * (kBK * 128) + key * 128 +
+                                            ((((col & 63) >> 3) ^ (key & 7)) << 4));
+          uint32_t r0, r1, r2, r3;
+          tc::ldmatrix_x4_trans(src, r0, r1, r2, r3);
+          // r[i] now holds the fragment of block i's transpose (rows = columns of V)
+          const int vrow = cb * 8 + k8;  // lane 8i + k8 stores row k8 of transposed block i
+          const int kk = kb * 8;         // its 8 keys
+          const uint32_t dst = tc::smem_u32(vdst + (kk >> 6) * (DH * 128) + vrow * 128 +
+                                            ((((kk & 63) >> 3) ^ (vrow & 7)) << 4));
+          tc::stmatrix_x4(dst, r0, r1, r2, r3);
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&vt_full[s]);
+          tc::mbar_arrive(v_empty);
+        }
       }
     }
   }
@@ -509,7 +544,10 @@ static cudaError_t launch_attn_t(const __half* q, const __half* k, const __half*
   a.n_qt = (T + kBQ - 1) / kBQ;
   a.wait_ns = wait_ns;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(a.n_qt * B * H));
+  int dev_sms = 148;
+  cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = (long long)a.n_qt * B * H;
+  cfg.gridDim = dim3((unsigned)(tiles < dev_sms ? tiles : dev_sms));  // persistent: one CTA per SM
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = st;
