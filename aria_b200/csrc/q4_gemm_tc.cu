@@ -823,7 +823,8 @@ static size_t tc_ws_bytes(int N, int M, int bt, int splits) {
 // Token-tile height BT and K split by a cost model: rounds of CTAs (work units
 // / SMs, rounded up) x 128-k stages per unit x (fixed issue cost of a stage + 4
 // cycles per token), plus, for a single accumulator, the exposed epilogue of
-// every round after the first, plus, for a K split, each unit's partial write
+// every round after the first (epi_per_token cycles per token of the tile),
+// plus, for a K split, each unit's partial write
 // and the last unit's reduction (measured: 7-9 us per round at 64 tokens, fit
 // as 10000 + 16 * S * BT in the same units).  The fixed ~640 cycles per stage
 // is the MMA issuer's latency (two barrier waits, a fence, eight MMAs and two
@@ -833,7 +834,15 @@ static size_t tc_ws_bytes(int N, int M, int bt, int splits) {
 // on ties, i.e. when the tiles fit one round) or two (the epilogue overlapped;
 // measured on B200 at M = 4096: Efkolos LM head 255 -> 248 us, config-4
 // ffn_down 508 -> 499 us, where the model picks it).
-static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail, int epi_per_token = 8) {
+// cycles per token of a tile's epilogue, exposed after every round but the
+// first when the tile has a single accumulator (measured with clock64 stamps in
+// the MMA thread on B200: ~16k cycles per 256-token tile, with or without GELU;
+// planning with it moved config-4 and Efkolos prefill shapes to double-buffered
+// tiles: config-4 LM head at M = 4096 0.924 -> 0.732 ms, Efkolos prefill step
+// 2.50 -> 2.35 ms)
+constexpr int kTcEpiCyclesPerToken = 60;
+
+static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail, int epi_per_token = kTcEpiCyclesPerToken) {
   struct Cand { int bt, nacc; };
   const Cand cands[] = {{64, 2}, {128, 2}, {192, 1}, {224, 1}, {256, 1}, {192, 2}};
   const int splits_c[] = {1, 2, 3, 4, 6, 8};  // the reduction unrolls up to 8 slices
@@ -902,10 +911,7 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   const size_t esz = (ydt & kOutF16) ? 2 : 4;
   const bool tma_ok = ((uintptr_t)y & 15u) == 0 && ((size_t)ldy * esz) % 16 == 0;
   a.tma_epi = !tma_ok ? kEpiThreads : beta == 0.0f ? kEpiStore : beta == 1.0f ? kEpiAdd : kEpiThreads;
-  // the exposed epilogue of a single accumulator grows with GELU and the
-  // residual term's loads
-  const int epi = 8 + ((ydt & kOutGelu) ? 16 : 0) + (beta != 0.0f ? 8 : 0);
-  const TcPlan p = plan_tc(K, N, M, tc_num_sms(), workspace ? workspace_bytes : 0, epi);
+  const TcPlan p = plan_tc(K, N, M, tc_num_sms(), workspace ? workspace_bytes : 0);
   a.splits = p.splits;
   a.ws_part = nullptr;
   a.ws_cnt = nullptr;
