@@ -69,9 +69,10 @@ def parse():
     ap.add_argument("--launches", type=int, default=3, help="--case: launches before exiting")
     ap.add_argument("--kernel", default="auto", help="--case: auto, stream, register or tensor")
     ap.add_argument("--time", action="store_true", help="--case: also time the kind over weight copies")
-    ap.add_argument("--program", default=None, choices=["decode_step", "decode_kv"],
+    ap.add_argument("--program", default=None, choices=["decode_step", "decode_kv", "prefill_fwd"],
                     help="run one whole program --launches times (for ncu launch lists): the 81-projection "
-                         "step (decode_step, --M token rows) or the decode step with KV cache (decode_kv)")
+                         "step (decode_step, --M token rows), the decode step with KV cache (decode_kv) or the "
+                         "whole-prompt forward (prefill_fwd, --seqs x --M tokens)")
     return ap.parse_args()
 
 
@@ -283,6 +284,13 @@ def run_program(args) -> None:
     if args.program == "decode_step":
         prog = DecodeProgram(Q4Stack.build(EFKOLOS, seed=1), M=args.M, seed=2)
         run = prog.run
+    elif args.program == "prefill_fwd":
+        # whole-prompt forward of --seqs sequences x --M tokens
+        from aria_b200.decoder import Decoder, DecoderWeights
+        dec = Decoder(DecoderWeights(EFKOLOS, max_seq=max(512, args.M), seed=3), M=args.seqs)
+        tokens = torch.randint(0, EFKOLOS.vocab_size, (args.seqs, args.M), generator=torch.Generator().manual_seed(5))
+        dec.prefill(tokens)
+        run = lambda: dec.run_prefill(args.M)  # noqa: E731
     else:
         from aria_b200.decoder import Decoder, DecoderWeights
         dec = Decoder(DecoderWeights(EFKOLOS, max_seq=512, seed=3), M=args.M)
@@ -294,7 +302,7 @@ def run_program(args) -> None:
         run()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-    print(json.dumps({"program": args.program, "M": args.M, "runs": args.launches}), flush=True)
+    print(json.dumps({"program": args.program, "M": args.M, "seqs": args.seqs, "runs": args.launches}), flush=True)
 
 
 def run_case(args) -> None:
