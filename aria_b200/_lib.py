@@ -49,7 +49,7 @@ SIGNATURES = {
     "aria_layernorm_f32": (_I, [_P, _I, _I, _P, _P, _F, _P, _I, _P]),
     "aria_attention_decode": (_I, [_P, _I, _I, _I, _P, _P, _I, _P, _P, _P]),
     "aria_flash_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _F, _P]),
-    "aria_attention_prefill": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),
+    "aria_attention_prefill": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P]),
     "aria_p2p_alloc": (_I, [_SZ, _P]),
     "aria_p2p_free": (_I, [_P]),
     "aria_p2p_ipc_handle": (_I, [_P, _P]),

@@ -48,10 +48,13 @@ def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
 
 
 def attention_prefill(qkv: torch.Tensor, B: int, T: int, heads: int, out: torch.Tensor | None = None,
-                      want_lse: bool = False):
+                      want_lse: bool = False, k_cache: torch.Tensor | None = None,
+                      v_cache: torch.Tensor | None = None):
     """qkv: f16 [B*T][3d] (the QKV projection of B sequences of T tokens).
     Returns (out f16 [B*T][d] with the heads side by side, lse [B][heads][T] or
-    None); scale 1/sqrt(d / heads), causal within each sequence."""
+    None); scale 1/sqrt(d / heads), causal within each sequence.  k_cache,
+    v_cache (f16 [B][max_seq][d], both or neither): positions 0..T-1 of the
+    keys and values are written there in the same launch."""
     _check(qkv, "qkv")
     if qkv.dim() != 2 or qkv.shape[0] != B * T or qkv.shape[1] % 3 != 0:
         raise ValueError("qkv must be [B*T][3d]")
@@ -60,8 +63,19 @@ def attention_prefill(qkv: torch.Tensor, B: int, T: int, heads: int, out: torch.
         out = torch.empty(B * T, d, dtype=torch.float16, device=qkv.device)
     _check(out, "out", (B * T, d))
     lse = torch.empty(B, heads, T, dtype=torch.float32, device=qkv.device) if want_lse else None
+    max_seq = 0
+    if (k_cache is None) != (v_cache is None):
+        raise ValueError("k_cache and v_cache go together")
+    if k_cache is not None:
+        _check(k_cache, "k_cache")
+        _check(v_cache, "v_cache", k_cache.shape)
+        if k_cache.dim() != 3 or k_cache.shape[0] != B or k_cache.shape[2] != d:
+            raise ValueError("caches must be [B][max_seq][d]")
+        max_seq = k_cache.shape[1]
     call("aria_attention_prefill", qkv.data_ptr(), B, T, d, heads, out.data_ptr(),
-         lse.data_ptr() if lse is not None else None, _stream(qkv.device))
+         lse.data_ptr() if lse is not None else None,
+         k_cache.data_ptr() if k_cache is not None else None,
+         v_cache.data_ptr() if v_cache is not None else None, max_seq, _stream(qkv.device))
     return out, lse
 
 

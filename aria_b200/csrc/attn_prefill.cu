@@ -58,6 +58,7 @@ struct AttnArgs {
   float* lse;                      // optional [B][H][T] (natural log)
   int n_qt;                        // query tiles per sequence
   unsigned long long wait_ns;
+  int fill_cache;                  // store every K and V block into the caches (tm_kc, tm_vc)
 };
 
 template <int DH>
@@ -93,14 +94,15 @@ __device__ __forceinline__ AttnTile attn_tile(const AttnArgs& a, int t) {
 template <int DH>
 __global__ void __maxnreg__(168)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc,
+                        const __grid_constant__ CUtensorMap tm_vc, const AttnArgs a) {
   using L = AttnSmem<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_empty = q_full + 1;    // S MMA commit after a tile's last block
   uint64_t* k_full = q_empty + 1;    // [2]
-  uint64_t* k_empty = k_full + 2;    // [2] S MMA commit
+  uint64_t* k_empty = k_full + 2;    // [2] S MMA commit (+ transposer warp 0 when filling the caches)
   uint64_t* v_full = k_empty + 2;    // [1]
   uint64_t* v_empty = v_full + 1;    // [1] 2 transposer warps
   uint64_t* vt_full = v_empty + 1;   // [2] 2 transposer warps
@@ -129,7 +131,7 @@ __global__ void __maxnreg__(168)
     tc::mbar_init(q_empty, 1);
     for (int s = 0; s < 2; s++) {
       tc::mbar_init(&k_full[s], 1);
-      tc::mbar_init(&k_empty[s], 1);
+      tc::mbar_init(&k_empty[s], a.fill_cache ? 2 : 1);
       tc::mbar_init(&vt_full[s], 2);
       tc::mbar_init(&vt_empty[s], 1);
       tc::mbar_init(&s_full[s], 1);
@@ -464,12 +466,32 @@ __global__ void __maxnreg__(168)
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          tc::mbar_arrive(&vt_full[s]);
-          tc::mbar_arrive(v_empty);
+        if (lane == 0) tc::mbar_arrive(&vt_full[s]);
+        if (tw == 0 && lane == 0) {
+          // KV-cache fill: the block's K and V boxes go to the caches once, from
+          // the CTA whose query tile is the block's own (its diagonal block);
+          // the shared-memory buffers are released only after TMA has read them
+          if (a.fill_cache && j == tl.nb - 1) {
+            bool kok = tc::mbar_wait_or_abort(&k_full[s], (g >> 1) & 1, 2 * a.wait_ns, abort_flag) == tc::kWaitOk;
+            if (kok) {
+#pragma unroll
+              for (int c = 0; c < DH / 64; c++) {
+                tc::tma_store_4d(&tm_kc, 64 * c, tl.head, j * kBK, tl.seq, smem + L::kKOff + s * L::kKV + c * (kBK * 128));
+                tc::tma_store_4d(&tm_vc, 64 * c, tl.head, j * kBK, tl.seq, smem + L::kVOff + c * (kBK * 128));
+              }
+              tc::bulk_commit();
+              tc::bulk_wait_read<0>();
+            } else {
+              give_up(tc::kWaitAborted, tc::kErrTimeoutEmpty);
+            }
+          }
+          if (a.fill_cache) tc::mbar_arrive(&k_empty[s]);
         }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(v_empty);
       }
     }
+    if (tw == 0 && lane == 0 && a.fill_cache) tc::bulk_wait_all();  // the cache writes are complete
   }
 
   tc::tc_fence_before();
@@ -518,13 +540,24 @@ constexpr int kAttnMaxDevices = 64;
 template <int DH>
 static cudaError_t launch_attn_t(const __half* q, const __half* k, const __half* v, long long s_head, long long s_pos,
                                  long long s_seq, int B, int H, int T, float scale, __half* out, long long o_seq,
-                                 long long o_head, long long o_pos, float* lse, cudaStream_t st,
-                                 unsigned long long wait_ns) {
+                                 long long o_head, long long o_pos, float* lse, __half* k_cache, __half* v_cache,
+                                 int max_seq, cudaStream_t st, unsigned long long wait_ns) {
   using L = AttnSmem<DH>;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tkc, tvc;
   if (!attn_tmap(&tq, q, DH, H, T, B, s_head, s_pos, s_seq) || !attn_tmap(&tk, k, DH, H, T, B, s_head, s_pos, s_seq) ||
       !attn_tmap(&tv, v, DH, H, T, B, s_head, s_pos, s_seq))
     return cudaErrorInvalidValue;
+  // the caches [B][max_seq][H * DH]: positions 0 .. T - 1 written (the map's
+  // extent clips the rest of a partial block)
+  const bool fill = k_cache != nullptr && v_cache != nullptr;
+  memset(&tkc, 0, sizeof(tkc));
+  memset(&tvc, 0, sizeof(tvc));
+  if (fill) {
+    const long long d = (long long)H * DH;
+    if (!attn_tmap(&tkc, k_cache, DH, H, T, B, DH, d, (long long)max_seq * d) ||
+        !attn_tmap(&tvc, v_cache, DH, H, T, B, DH, d, (long long)max_seq * d))
+      return cudaErrorInvalidValue;
+  }
   auto kern = attn_prefill_kernel<DH>;
   static bool attr_set[kAttnMaxDevices] = {};
   int dev = 0;
@@ -543,6 +576,7 @@ static cudaError_t launch_attn_t(const __half* q, const __half* k, const __half*
   a.lse = lse;
   a.n_qt = (T + kBQ - 1) / kBQ;
   a.wait_ns = wait_ns;
+  a.fill_cache = fill ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   int dev_sms = 148;
   cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, dev);
@@ -556,22 +590,24 @@ static cudaError_t launch_attn_t(const __half* q, const __half* k, const __half*
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, a);
+  return cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, tkc, tvc, a);
 }
 
 // Causal attention of B sequences x H heads over T positions, head size DH (64
 // or 128): q / k / v element (seq, head, pos, i) at base + seq s_seq + head
 // s_head + pos s_pos + i, out likewise with its own strides, lse (optional)
-// [B][H][T].
+// [B][H][T]; with k_cache and v_cache ([B][max_seq][H * DH], optional) the
+// keys and values of positions 0 .. T - 1 are also written there.
 cudaError_t launch_attention_prefill(const __half* q, const __half* k, const __half* v, int DH, long long s_head,
                                      long long s_pos, long long s_seq, int B, int H, int T, float scale, __half* out,
-                                     long long o_seq, long long o_head, long long o_pos, float* lse, cudaStream_t st) {
+                                     long long o_seq, long long o_head, long long o_pos, float* lse,
+                                     __half* k_cache, __half* v_cache, int max_seq, cudaStream_t st) {
   if (DH == 64)
-    return launch_attn_t<64>(q, k, v, s_head, s_pos, s_seq, B, H, T, scale, out, o_seq, o_head, o_pos, lse, st,
-                             tc::kWaitLimitNs);
+    return launch_attn_t<64>(q, k, v, s_head, s_pos, s_seq, B, H, T, scale, out, o_seq, o_head, o_pos, lse, k_cache,
+                             v_cache, max_seq, st, tc::kWaitLimitNs);
   if (DH == 128)
-    return launch_attn_t<128>(q, k, v, s_head, s_pos, s_seq, B, H, T, scale, out, o_seq, o_head, o_pos, lse, st,
-                              tc::kWaitLimitNs);
+    return launch_attn_t<128>(q, k, v, s_head, s_pos, s_seq, B, H, T, scale, out, o_seq, o_head, o_pos, lse, k_cache,
+                              v_cache, max_seq, st, tc::kWaitLimitNs);
   return cudaErrorInvalidValue;
 }
 

@@ -36,7 +36,8 @@ cudaError_t launch_p2p_allreduce(const float* const* part, unsigned* const* flag
                                  int rank, __half* h, int n, unsigned long long wait_ns, cudaStream_t st);
 cudaError_t launch_attention_prefill(const __half* q, const __half* k, const __half* v, int DH, long long s_head,
                                      long long s_pos, long long s_seq, int B, int H, int T, float scale, __half* out,
-                                     long long o_seq, long long o_head, long long o_pos, float* lse, cudaStream_t st);
+                                     long long o_seq, long long o_head, long long o_pos, float* lse,
+                                     __half* k_cache, __half* v_cache, int max_seq, cudaStream_t st);
 cudaError_t launch_embed(const __half* embed, const __half* pos_embed, const int* tok, const int* pos, int M, int vocab,
                          int max_seq, int d, float* h, cudaStream_t st);
 cudaError_t launch_layernorm(const float* x, const __half* g, const __half* b, int M, int d, float eps, __half* y,
@@ -368,24 +369,28 @@ int aria_flash_attn_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   // [NH][T][dh]: one head per "sequence" of the kernel's 4-D view
   const long long st = (long long)T * dh;
   return cuda_status(launch_attention_prefill((const __half*)q, (const __half*)k, (const __half*)v, dh, dh, dh, st,
-                                              NH, 1, T, scale, (__half*)out, st, 0, dh, lse, (cudaStream_t)stream));
+                                              NH, 1, T, scale, (__half*)out, st, 0, dh, lse, nullptr, nullptr, 0,
+                                              (cudaStream_t)stream));
 }
 
 int aria_attention_prefill(const uint16_t* qkv, int B, int T, int d, int heads, uint16_t* out, float* lse,
-                           void* stream) {
+                           uint16_t* k_cache, uint16_t* v_cache, int max_seq, void* stream) {
   if (B < 0 || T < 0 || d <= 0 || heads <= 0 || d % heads != 0 || d % 8 != 0) return ARIA_Q4_EINVAL;
   const int dh = d / heads;
   if (dh != 64 && dh != 128) return ARIA_Q4_EUNSUPPORTED;
+  if ((k_cache == nullptr) != (v_cache == nullptr)) return ARIA_Q4_EINVAL;
+  if (k_cache && max_seq < T) return ARIA_Q4_ESIZE;
   if (B == 0 || T == 0) return ARIA_Q4_OK;
   if (!qkv || !out) return ARIA_Q4_EINVAL;
   if (!aligned16(qkv) || !aligned16(out)) return ARIA_Q4_EALIGN;
+  if (k_cache && (!aligned16(k_cache) || !aligned16(v_cache))) return ARIA_Q4_EALIGN;
   if ((long long)B * heads * ((T + 127) / 128) > 0x7fffffffLL) return ARIA_Q4_ESIZE;
   if (int s = check_device()) return s;
   const __half* q = (const __half*)qkv;
   const long long row = 3LL * d;
   return cuda_status(launch_attention_prefill(q, q + d, q + 2 * d, dh, dh, row, row * T, B, heads, T,
                                               1.0f / sqrtf((float)dh), (__half*)out, (long long)T * d, dh, d, lse,
-                                              (cudaStream_t)stream));
+                                              (__half*)k_cache, (__half*)v_cache, max_seq, (cudaStream_t)stream));
 }
 
 // ------------------------------------------------------------------ failure-path test hook

@@ -319,6 +319,13 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, con
                "r"(x), "r"(y), "r"(smem_u32(src))
                : "memory");
 }
+// 4-D tiled TMA store of a shared-memory box (bulk async-group of the issuing thread).
+__device__ __forceinline__ void tma_store_4d(const void* tmap, int c0, int c1, int c2, int c3, const void* src) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(tmap),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
+      : "memory");
+}
 __device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, int x, int y, const void* src) {
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                    tmap),

@@ -210,8 +210,9 @@ class Decoder:
         prompt (aria_attention_prefill) -> attn_out into the f32 residual ->
         LayerNorm -> ffn_up + GELU -> ffn_down into the residual, then the final
         LayerNorm and the LM head over every token (f16 logits [M*T][vocab]).
-        With fill_cache, each layer's k and v rows are copied into the KV caches
-        at positions 0..T-1, so `step` continues at position T."""
+        With fill_cache, each layer's attention launch also stores its k and v
+        rows into the KV caches at positions 0..T-1, so `step` continues at
+        position T."""
         from .attention import attention_prefill
         cfg, w, b = self.cfg, self.w, self._prefill_buffers(T)
         d, n = cfg.d_model, self.M * T
@@ -227,11 +228,10 @@ class Decoder:
         for i, p in enumerate(w.layers):
             ln(p.ln1_g, p.ln1_b)
             matmul(b["xn"], p.qkv, b["qkv"], bias=p.b_qkv, const_weights=True)
-            attention_prefill(b["qkv"], self.M, T, cfg.num_heads, out=b["att"])
-            if fill_cache:
-                qkv3 = b["qkv"].view(self.M, T, 3 * d)
-                self.k_cache[i][:, :T].copy_(qkv3[:, :, d:2 * d])
-                self.v_cache[i][:, :T].copy_(qkv3[:, :, 2 * d:])
+            # the attention launch also stores this layer's k, v rows into the caches
+            attention_prefill(b["qkv"], self.M, T, cfg.num_heads, out=b["att"],
+                              k_cache=self.k_cache[i] if fill_cache else None,
+                              v_cache=self.v_cache[i] if fill_cache else None)
             matmul(b["att"], p.out, b["h"], bias=p.b_out, beta=1.0, const_weights=True)
             ln(p.ln2_g, p.ln2_b)
             matmul(b["xn"], p.up, b["u"], bias=p.b_up, activation="gelu", const_weights=True)
@@ -252,9 +252,8 @@ class Decoder:
         return self.run_prefill(T, fill_cache)
 
     def prefill_launches(self, fill_cache: bool = True) -> int:
-        """Kernels of one run_prefill (the cache copies are torch copy kernels)."""
-        per_layer = 7 + (2 if fill_cache else 0)
-        return 1 + per_layer * self.cfg.num_layers + 2
+        """Kernels of one run_prefill."""
+        return 1 + 7 * self.cfg.num_layers + 2
 
 
 __all__ = ["Decoder", "DecoderWeights", "sinusoidal_positions", "LN_EPS"]

@@ -265,9 +265,13 @@ ARIA_Q4_API int aria_flash_attn_fwd(const uint16_t* q, const uint16_t* k, const 
  * h at columns h dh, d + h dh, 2 d + h dh), out f16 [B * T][d] with the heads
  * side by side -- the layout attn_out reads (forward_gpu's attention block,
  * src/transformer_cuda.rs:1583-1686).  scale 1/sqrt(dh); lse [B][heads][T] or
- * NULL.  dh = d / heads 64 or 128; d a multiple of 8; qkv, out 16-byte aligned. */
+ * NULL.  k_cache, v_cache (both or neither; f16 [B][max_seq][d], max_seq >= T):
+ * the keys and values of positions 0 .. T - 1 are also stored there, as the
+ * decode step's caches hold them (the reference's KVCache,
+ * src/transformer_cuda.rs:144-155), in the same launch.  dh = d / heads 64 or
+ * 128; d a multiple of 8; qkv, out and the caches 16-byte aligned. */
 ARIA_Q4_API int aria_attention_prefill(const uint16_t* qkv, int B, int T, int d, int heads, uint16_t* out,
-                                       float* lse, void* stream);
+                                       float* lse, uint16_t* k_cache, uint16_t* v_cache, int max_seq, void* stream);
 
 /* ---------------------------------------------------------------- multi-GPU */
 

@@ -51,13 +51,37 @@ def test_attention_prefill_packed_qkv(B, T, d, heads):
     assert _lib.lib().aria_q4_take_device_error() == 0
 
 
+@pytest.mark.parametrize("B,T,d,heads,max_seq", [(3, 200, 896, 14, 256), (2, 128, 256, 2, 300), (1, 5, 512, 8, 5)])
+def test_attention_prefill_fills_kv_cache(B, T, d, heads, max_seq):
+    """With caches, the same launch stores positions 0..T-1 of k and v into
+    [B][max_seq][d] (bit-exact copies of the QKV columns) and leaves the rest of
+    the caches untouched; the attention output is unchanged."""
+    from aria_b200.attention import attention_prefill
+    qkv = torch.from_numpy(_rand((B * T, 3 * d), 7 * T + d)).cuda()
+    kc = torch.full((B, max_seq, d), 3.0, dtype=torch.float16, device="cuda")
+    vc = torch.full((B, max_seq, d), -3.0, dtype=torch.float16, device="cuda")
+    out_a, _ = attention_prefill(qkv, B, T, heads)
+    out_b, _ = attention_prefill(qkv, B, T, heads, k_cache=kc, v_cache=vc)
+    torch.cuda.synchronize()
+    assert torch.equal(out_a, out_b)
+    q3 = qkv.view(B, T, 3 * d)
+    assert torch.equal(kc[:, :T], q3[:, :, d:2 * d]) and torch.equal(vc[:, :T], q3[:, :, 2 * d:])
+    assert bool((kc[:, T:] == 3.0).all()) and bool((vc[:, T:] == -3.0).all())
+
+
 def test_attention_rejects_bad_arguments():
     from aria_b200 import _lib
     lib = _lib.lib()
     x = torch.zeros(4, 3 * 96, dtype=torch.float16, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
-    assert lib.aria_attention_prefill(x.data_ptr(), 1, 4, 96, 3, x.data_ptr(), None, s) == _lib.EUNSUPPORTED  # dh 32
-    assert lib.aria_attention_prefill(x.data_ptr(), 1, 4, 96, 5, x.data_ptr(), None, s) == _lib.EINVAL  # d % heads
+    assert lib.aria_attention_prefill(x.data_ptr(), 1, 4, 96, 3, x.data_ptr(), None, None, None, 0,
+                                      s) == _lib.EUNSUPPORTED  # dh 32
+    assert lib.aria_attention_prefill(x.data_ptr(), 1, 4, 96, 5, x.data_ptr(), None, None, None, 0,
+                                      s) == _lib.EINVAL  # d % heads
+    assert lib.aria_attention_prefill(x.data_ptr(), 1, 4, 128, 2, x.data_ptr(), None, x.data_ptr(), None, 8,
+                                      s) == _lib.EINVAL  # one cache without the other
+    assert lib.aria_attention_prefill(x.data_ptr(), 1, 4, 128, 2, x.data_ptr(), None, x.data_ptr(), x.data_ptr(), 3,
+                                      s) == _lib.ESIZE  # cache shorter than the prompt
     assert lib.aria_flash_attn_fwd(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), None, 1, 4, 48, 0.1,
                                    s) == _lib.EUNSUPPORTED
     assert lib.aria_flash_attn_fwd(x.data_ptr() + 2, x.data_ptr(), x.data_ptr(), x.data_ptr(), None, 1, 4, 64, 0.1,
