@@ -345,9 +345,17 @@ __global__ void __maxnreg__(168)
           tc::tmem_ld_32x32b_x32(scol, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
           tc::tmem_ld_32x32b_x32(scol + 32u, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
           tc::tmem_ld_wait();
+          // a tree, not a chain of 64 dependent maxima
+          float m8[8];
 #pragma unroll
-          for (int e = 0; e < 64; e++)
-            if (e <= kmax) mx = fmaxf(mx, __uint_as_float(sv[e]));
+          for (int u = 0; u < 8; u++) {
+            float t = -INFINITY;
+#pragma unroll
+            for (int e = u; e < 64; e += 8)
+              if (e <= kmax) t = fmaxf(t, __uint_as_float(sv[e]));
+            m8[u] = t;
+          }
+          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         }
         mx *= a.scale_log2;  // scale > 0: the maximum commutes with it
         float* rd = red + (g & 1) * (2 * kBQ);
@@ -363,7 +371,7 @@ __global__ void __maxnreg__(168)
         // half's own S columns (keys hf*64 + 16u .. +15 -> columns hf*64 + 8u ..
         // +7), which it has read already; the O product addresses its A slices
         // there.  32 scores per TMEM wait.
-        float sum = 0.0f;
+        float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four independent chains of additions
 #pragma unroll
         for (int c = 0; c < 2; c++) {
           uint32_t sv[32];
@@ -378,7 +386,7 @@ __global__ void __maxnreg__(168)
             const float x1 = k + 1 <= kmax ? fmaf(__uint_as_float(sv[2 * e + 1]), a.scale_log2, -msub) : -INFINITY;
             const float p0 = tc::ex2_approx(x0);
             const float p1 = tc::ex2_approx(x1);
-            sum += p0 + p1;
+            sum4[e & 3] += p0 + p1;
             const __half2 h2 = __floats2half2_rn(p0, p1);
             pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
           }
@@ -388,7 +396,7 @@ __global__ void __maxnreg__(168)
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&p_full[b]);
-        l = fmaf(l, alpha, sum);
+        l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
         if (j >= 1) accumulate(g - 1, alpha_prev);
         alpha_prev = alpha;
       }

@@ -93,9 +93,9 @@ constexpr int kQDepth = 4;  // 128-k code groups in flight per dequant warpgroup
 // its scales (NK: 8 B per row; KN: 256 B per 32-row group)
 constexpr int kQSlot = 128 * 64;
 constexpr int kSSlot = 128 * 8 > 4 * 256 ? 128 * 8 : 4 * 256;
-// staged epilogue: per epilogue warp, two 1-KB boxes of [16 tokens][32 rows]
-// f16 or [8 tokens][32 rows] f32
-constexpr int kEChunk = 1024;
+// staged epilogue: per epilogue warp, one 2-KB box of [32 tokens][32 rows] f16
+// or [16 tokens][32 rows] f32
+constexpr int kEChunk = 1024;  // the box is two of these
 
 template <int BT, int STAGES>
 struct TcSmem {
@@ -507,9 +507,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // GELU and writes a [tokens][32 rows] box to shared memory, which lane 0
         // hands to TMA -- a store, or for the residual term (beta = 1) an
         // add-reduction performed at L2, so no old value is ever loaded.  f16:
-        // 16-token chunks, f16 pairs along tokens packed and transposed by
+        // 32-token chunks, f16 pairs along tokens packed and transposed by
         // stmatrix (256 outputs each), 64-byte rows with 64-byte swizzle
-        // (16-byte chunk c of row k at c ^ ((k >> 1) & 3)); f32: 8-token
+        // (16-byte chunk c of row k at c ^ ((k >> 1) & 3)); f32: 16-token
         // chunks, 128-byte rows, 128-byte swizzle.  Rows and tokens outside the
         // tensor are clipped by TMA.
         const int g = lane >> 2, t4 = lane & 3;
@@ -524,97 +524,100 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const bool gelu = (a.ydt & kOutGelu) != 0;
         const bool add = a.tma_epi == kEpiAdd;
         if (a.ydt & kOutF16) {
-          // 16-token chunks ([16 tokens][32 rows] boxes of 1 KB): two stmatrix
-          // per chunk, half the per-chunk fences and TMA issues of 8-token ones
-          // (measured: the Efkolos prefill chain at M = 4096 took 2.48 ms with
-          // 16-token and 2.96 ms with 8-token chunks)
+          // 32-token chunks, one 2 KB box per warp, rewritten once TMA has read
+          // it (measured: the Efkolos prefill chain at M = 4096 took 2.35 ms with
+          // two alternating 16-token boxes, 2.15 ms with this; 2.96 ms with
+          // 8-token boxes): the per-chunk fence, warp sync and TMA issue dominate
 #pragma unroll 1
-          for (int c = 0; c < BT / 16 && m0 + c * 16 < a.M; c++) {
-            uint32_t v[2][8];
-            tc::tmem_ld_16x256b_x2(tmem_d + (uint32_t)(c * 16), v[0]);
-            tc::tmem_ld_16x256b_x2(tmem_d + (16u << 16) + (uint32_t)(c * 16), v[1]);
-            tc::tmem_ld_wait();
-            uint32_t pk[2][4];
+          for (int c = 0; c < BT / 32 && m0 + c * 32 < a.M; c++) {
+            uint32_t pk[2][2][4];
 #pragma unroll
-            for (int h = 0; h < 2; h++)
+            for (int hh = 0; hh < 2; hh++) {
+              uint32_t v[2][8];
+              tc::tmem_ld_16x256b_x2(tmem_d + (uint32_t)(c * 32 + hh * 16), v[0]);
+              tc::tmem_ld_16x256b_x2(tmem_d + (16u << 16) + (uint32_t)(c * 32 + hh * 16), v[1]);
+              tc::tmem_ld_wait();
 #pragma unroll
-              for (int e = 0; e < 4; e++) {
-                // v[h][2e], v[h][2e+1]: row 16h + 8 (e & 1) + g of the warp, tokens 8 (e >> 1) + 2 t4, +1
-                const float b = bz[2 * h + (e & 1)];
-                float lo = fmaf(a.alpha, __uint_as_float(v[h][2 * e]), b);
-                float hi = fmaf(a.alpha, __uint_as_float(v[h][2 * e + 1]), b);
-                if (gelu) {
-                  lo = gelu_fast(lo);
-                  hi = gelu_fast(hi);
+              for (int h = 0; h < 2; h++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                  // v[h][2e], v[h][2e+1]: row 16h + 8 (e & 1) + g of the warp,
+                  // tokens 16 hh + 8 (e >> 1) + 2 t4, +1
+                  const float b = bz[2 * h + (e & 1)];
+                  float lo = fmaf(a.alpha, __uint_as_float(v[h][2 * e]), b);
+                  float hi = fmaf(a.alpha, __uint_as_float(v[h][2 * e + 1]), b);
+                  if (gelu) {
+                    lo = gelu_fast(lo);
+                    hi = gelu_fast(hi);
+                  }
+                  const __half2 p2 = __floats2half2_rn(lo, hi);
+                  pk[hh][h][e] = *reinterpret_cast<const uint32_t*>(&p2);
                 }
-                const __half2 p2 = __floats2half2_rn(lo, hi);
-                pk[h][e] = *reinterpret_cast<const uint32_t*>(&p2);
-              }
-            uint8_t* eb = ebuf + (c & 1) * kEChunk;
-            if (c >= 2) {
-              if (lane == 0) tc::bulk_wait_read<1>();  // the box written two chunks ago has been read
+            }
+            if (c >= 1) {
+              if (lane == 0) tc::bulk_wait_read<0>();  // the previous box has been read
               __syncwarp();
             }
-            // matrix i = (rows 8 (i & 1) .. +7 of half h, tokens 8 (i >> 1) .. +7);
-            // lane 8i + k addresses its column k, i.e. token k + 8 (i >> 1)
-            const int mi = lane >> 3, tk = (lane & 7) + 8 * (mi >> 1);
+            // matrix mi = (rows 8 (mi & 1) .. +7 of half h, tokens 16 hh + 8 (mi >> 1) .. +7);
+            // lane 8 mi + k addresses its column k
+            const int mi = lane >> 3;
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-              const int chunk = 2 * h + (mi & 1);
-              tc::stmatrix_x4_trans(tc::smem_u32(eb + tk * 64 + ((chunk ^ ((tk >> 1) & 3)) << 4)), pk[h][0],
-                                    pk[h][1], pk[h][2], pk[h][3]);
+            for (int hh = 0; hh < 2; hh++) {
+              const int tk = hh * 16 + (lane & 7) + 8 * (mi >> 1);
+#pragma unroll
+              for (int h = 0; h < 2; h++) {
+                const int chunk = 2 * h + (mi & 1);
+                tc::stmatrix_x4_trans(tc::smem_u32(ebuf + tk * 64 + ((chunk ^ ((tk >> 1) & 3)) << 4)), pk[hh][h][0],
+                                      pk[hh][h][1], pk[hh][h][2], pk[hh][h][3]);
+              }
             }
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
               if (add)
-                tc::tma_reduce_add_2d(&tmap_y, nq, m0 + c * 16, eb);
+                tc::tma_reduce_add_2d(&tmap_y, nq, m0 + c * 32, ebuf);
               else
-                tc::tma_store_2d(&tmap_y, nq, m0 + c * 16, eb);
+                tc::tma_store_2d(&tmap_y, nq, m0 + c * 32, ebuf);
               tc::bulk_commit();
             }
           }
         } else {
-          // f32: 16-byte chunk c of token row k at c ^ k; each value is one
-          // 4-byte shared store, conflict-free (a warp's 32 stores cover 8 rows x
-          // 4 tokens in distinct banks)
-          const int nch = min(BT / 8, (a.M - m0 + 7) / 8);
-          uint32_t v[2][4];
-          tc::tmem_ld_16x256b_x1(tmem_d, v[0]);
-          tc::tmem_ld_16x256b_x1(tmem_d + (16u << 16), v[1]);
-          tc::tmem_ld_wait_regs(v[0], v[1]);
+          // f32: 16-token chunks, one 2 KB box [16 tokens][32 rows] (128-byte
+          // rows, 128-byte swizzle: 16-byte chunk c of token row k at c ^ (k & 7));
+          // each value is one 4-byte shared store, conflict-free (a warp's 32
+          // stores cover 8 rows x 4 tokens in distinct banks)
 #pragma unroll 1
-          for (int c = 0; c < nch; c++) {
-            if (c > 0) {
-              tc::tmem_ld_16x256b_x1(tmem_d + (uint32_t)(c * 8), v[0]);
-              tc::tmem_ld_16x256b_x1(tmem_d + (16u << 16) + (uint32_t)(c * 8), v[1]);
-              tc::tmem_ld_wait_regs(v[0], v[1]);
-            }
-            uint8_t* eb = ebuf + (c & 1) * kEChunk;
-            if (c >= 2) {
-              if (lane == 0) tc::bulk_wait_read<1>();
+          for (int c = 0; c < BT / 16 && m0 + c * 16 < a.M; c++) {
+            if (c >= 1) {
+              if (lane == 0) tc::bulk_wait_read<0>();
               __syncwarp();
             }
+#pragma unroll 1
+            for (int hh = 0; hh < 2; hh++) {  // two 8-token halves of the box
+              uint32_t v[2][4];
+              tc::tmem_ld_16x256b_x1(tmem_d + (uint32_t)(c * 16 + hh * 8), v[0]);
+              tc::tmem_ld_16x256b_x1(tmem_d + (16u << 16) + (uint32_t)(c * 16 + hh * 8), v[1]);
+              tc::tmem_ld_wait();
 #pragma unroll
-            for (int h = 0; h < 2; h++)
+              for (int h = 0; h < 2; h++)
 #pragma unroll
-              for (int e = 0; e < 4; e++) {
-                // v[h][e]: row 16h + 8 (e >> 1) + g of the warp, token 2 t4 + (e & 1)
-                const int row = 16 * h + 8 * (e >> 1) + g, tk = 2 * t4 + (e & 1);
-                float o = fmaf(a.alpha, __uint_as_float(v[h][e]), bz[2 * h + (e >> 1)]);
-                if (gelu) o = gelu_fast(o);
-                *reinterpret_cast<float*>(eb + tk * 128 + ((((row >> 2) ^ tk) & 7) << 4) + (row & 3) * 4) = o;
-              }
+                for (int e = 0; e < 4; e++) {
+                  // v[h][e]: row 16h + 8 (e >> 1) + g of the warp, token 8 hh + 2 t4 + (e & 1)
+                  const int row = 16 * h + 8 * (e >> 1) + g, tk = 8 * hh + 2 * t4 + (e & 1);
+                  float o = fmaf(a.alpha, __uint_as_float(v[h][e]), bz[2 * h + (e >> 1)]);
+                  if (gelu) o = gelu_fast(o);
+                  *reinterpret_cast<float*>(ebuf + tk * 128 + ((((row >> 2) ^ tk) & 7) << 4) + (row & 3) * 4) = o;
+                }
+            }
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
               if (add)
-                tc::tma_reduce_add_2d(&tmap_y, nq, m0 + c * 8, eb);
+                tc::tma_reduce_add_2d(&tmap_y, nq, m0 + c * 16, ebuf);
               else
-                tc::tma_store_2d(&tmap_y, nq, m0 + c * 8, eb);
+                tc::tma_store_2d(&tmap_y, nq, m0 + c * 16, ebuf);
               tc::bulk_commit();
             }
-
           }
         }
         tc::tc_fence_before();
@@ -758,15 +761,15 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  // output boxes of the staged epilogue: [16 tokens][32 rows] f16 with 64-byte
-  // swizzle or [8 tokens][32 rows] f32 with 128-byte swizzle
+  // output boxes of the staged epilogue: [32 tokens][32 rows] f16 with 64-byte
+  // swizzle or [16 tokens][32 rows] f32 with 128-byte swizzle (2 KB each)
   CUtensorMap tmy;
   memset(&tmy, 0, sizeof(tmy));
   if (a.tma_epi != kEpiThreads) {
     const cuuint64_t ydim[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     const bool f16 = (a.ydt & kOutF16) != 0;
     const cuuint64_t ystride[1] = {(cuuint64_t)a.ldy * (f16 ? 2 : 4)};
-    const cuuint32_t ybox[2] = {32u, f16 ? 16u : 8u};
+    const cuuint32_t ybox[2] = {32u, f16 ? 32u : 16u};
     r = enc(&tmy, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, ydim, ystride, ybox,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, f16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
