@@ -6,10 +6,10 @@ host has already raised (no waiting), or one that nothing ever raises (the wait
 must run out within its limit, record ARIA_Q4_DEVERR_PEER_TIMEOUT and leave h
 unchanged).  Only one kernel runs at a time; nothing waits on another launch.
 
-On two GPUs (skipped with fewer): two processes, NCCL for the set-up and the
-logits all-gather, the column-split decode with the peer reduction against
-the same program with NCCL's all-reduce, and a second step (graph-free) to
-check that the per-call epochs stay in step."""
+On 2-8 GPUs (skipped with fewer): one process per GPU, NCCL for the set-up
+and the logits all-gather, the column-split decode with the peer reduction
+against the same program with NCCL's all-reduce, and a second step
+(graph-free) to check that the per-call epochs stay in step."""
 import ctypes
 import os
 
@@ -137,12 +137,14 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpus_peer_reduction_matches_nccl():
+def test_multi_gpu_peer_reduction_matches_nccl():
+    """Every visible GPU (2..8) as one rank."""
     import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29500 + os.getpid() % 1000
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=600) for _ in procs]
