@@ -192,18 +192,51 @@ __global__ void __launch_bounds__(256, 2) decode_mma_kernel(const DecodeArgs a) 
     // LayerNorm statistics of this CTA's token rows, one warp per row: the
     // mean, then the mean of the centred squares (two passes, as the
     // reference's cpu_layernorm_stats, lold3344/ARIA src/transformer_cuda.rs:3276-3293)
+    // (h is 16-byte aligned with ldx and K multiples of 4: float4 loads).
+    // Rows of up to 1024 values are held in registers, so both passes cost
+    // one round of loads; longer rows are read twice.
     const int nrow = min(8 * NT, a.M - m0);
+    const int n4 = a.K >> 2;
     for (int tl = warp; tl < nrow; tl += 8) {
-      const float* hr = a.h + (size_t)(m0 + tl) * a.ldx;
-      float sum = 0.0f;
-      for (int k = lane; k < a.K; k += 32) sum += hr[k];
+      const float4* hr = reinterpret_cast<const float4*>(a.h + (size_t)(m0 + tl) * a.ldx);
+      float sum = 0.0f, sq = 0.0f, mean;
+      if (n4 <= 8 * 32) {
+        float4 v[8];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      const float mean = sum / (float)a.K;
-      float sq = 0.0f;
-      for (int k = lane; k < a.K; k += 32) {
-        const float c = hr[k] - mean;
-        sq = fmaf(c, c, sq);
+        for (int i = 0; i < 8; i++) {
+          const int c = lane + 32 * i;
+          v[i] = c < n4 ? __ldg(hr + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mean = sum / (float)a.K;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (lane + 32 * i < n4) {
+            const float c0 = v[i].x - mean, c1 = v[i].y - mean, c2 = v[i].z - mean, c3 = v[i].w - mean;
+            sq = fmaf(c0, c0, sq);
+            sq = fmaf(c1, c1, sq);
+            sq = fmaf(c2, c2, sq);
+            sq = fmaf(c3, c3, sq);
+          }
+        }
+      } else {
+        for (int c = lane; c < n4; c += 32) {
+          const float4 v = __ldg(hr + c);
+          sum += (v.x + v.y) + (v.z + v.w);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mean = sum / (float)a.K;
+        for (int c = lane; c < n4; c += 32) {
+          const float4 v = __ldg(hr + c);
+          const float c0 = v.x - mean, c1 = v.y - mean, c2 = v.z - mean, c3 = v.w - mean;
+          sq = fmaf(c0, c0, sq);
+          sq = fmaf(c1, c1, sq);
+          sq = fmaf(c2, c2, sq);
+          sq = fmaf(c3, c3, sq);
+        }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
