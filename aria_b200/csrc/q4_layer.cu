@@ -97,15 +97,16 @@ __global__ void __launch_bounds__(kLayerThreads) layernorm_kernel(const float* x
 }
 
 // One CTA per (sequence m, head hd), head dimension DH.  qkv [M][3d] f16 holds
-// this token's q, k, v; the caches are f16 [M][max_seq][d].  The new k, v are
-// written at pos[m] first; then every thread scores whole positions (the k
-// row's DH/8 16-byte loads issued before the first multiply, q in shared
-// memory), the scores are softmaxed in f32 (max-subtracted), and the weighted
-// sum of V is formed by (head dimension pair, position group) threads, 16
-// positions' values loaded before their multiply-adds.  Loads are batched
-// because a load feeding the next multiply-add of a chain would otherwise
-// wait out one memory round trip per cached position.  scores: shared memory
-// of max_seq floats.
+// this token's q, k, v; the caches are f16 [M][max_seq][d].  The token's own
+// k, v are read from the qkv row and stored at pos[m] in the caches (for the
+// following steps); positions 0..pos-1 come from the caches.  Nothing waits
+// on that store, so the dependent loads are: the position, then every K row
+// (a thread per position, DH/8 16-byte loads issued before the first
+// multiply; the V rows are prefetched into L2 at the same time), then the V
+// values.  Scores are softmaxed in f32 (max-subtracted) in shared memory and
+// the weighted sum of V is formed by (head dimension pair, position group)
+// threads, 16 positions' values loaded before their multiply-adds.  scores:
+// shared memory of max_seq floats.
 template <int DH>
 __global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* qkv, int d, int max_seq,
                                                                   const int* pos, __half* kc, __half* vc,
@@ -116,27 +117,48 @@ __global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* 
   float* part = qs + DH;
   __shared__ float red[32];
   const int m = blockIdx.x, hd = blockIdx.y, tid = threadIdx.x;
+  const __half* row = qkv + (size_t)m * 3 * d;
+  const __half* qn = row + hd * DH;          // this token's q, k, v for the head
+  const __half* kn = row + d + hd * DH;
+  const __half* vn = row + 2 * d + hd * DH;
+  __half qe = __float2half_rn(0.0f), ke = qe, ve = qe;
+  if (tid < DH) {  // DH <= kLayerThreads: one element each, loaded alongside the position
+    qe = qn[tid];
+    ke = kn[tid];
+    ve = vn[tid];
+  }
   const int p = pos[m];
   if (p < 0 || p >= max_seq) {  // no cache slot: the caller's position is out of range
     for (int j = tid; j < DH; j += blockDim.x) out[(size_t)m * d + hd * DH + j] = __float2half_rn(0.0f);
     return;
   }
-  const __half* row = qkv + (size_t)m * 3 * d;
   __half* kcm = kc + (size_t)m * max_seq * d + hd * DH;
   __half* vcm = vc + (size_t)m * max_seq * d + hd * DH;
-  for (int j = tid; j < DH; j += blockDim.x) {
-    qs[j] = __half2float(row[hd * DH + j]);
-    kcm[(size_t)p * d + j] = row[d + hd * DH + j];
-    vcm[(size_t)p * d + j] = row[2 * d + hd * DH + j];
-  }
-  __syncthreads();  // the new k, v are in the cache (read back below by other threads)
   const int n = p + 1;
-  float mx = -INFINITY;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kcm + (size_t)i * d);  // 8 halves per load
-    uint4 kw[DH / 8];
+  auto krow = [&](int i) -> const uint4* {
+    return reinterpret_cast<const uint4*>(i == p ? kn : kcm + (size_t)i * d);
+  };
+  // first position of this thread: its K row in flight before anything else
+  uint4 kw[DH / 8];
+  if (tid < n) {
+    const uint4* kr = krow(tid);
 #pragma unroll
     for (int j = 0; j < DH / 8; j++) kw[j] = kr[j];
+  }
+  for (int i = tid; i < p; i += blockDim.x) bulk_prefetch_l2(vcm + (size_t)i * d, DH * 2);
+  if (tid < DH) {
+    qs[tid] = __half2float(qe);
+    kcm[(size_t)p * d + tid] = ke;
+    vcm[(size_t)p * d + tid] = ve;
+  }
+  __syncthreads();  // qs
+  float mx = -INFINITY;
+  for (int i = tid; i < n; i += blockDim.x) {
+    if (i != tid) {
+      const uint4* kr = krow(i);
+#pragma unroll
+      for (int j = 0; j < DH / 8; j++) kw[j] = kr[j];
+    }
     float dot = 0.0f;
 #pragma unroll
     for (int j = 0; j < DH / 8; j++) {
@@ -165,12 +187,13 @@ __global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* 
   // 16 positions' pairs loaded before their multiply-adds
   constexpr int kPairs = DH / 2, kGroups = kLayerThreads / kPairs;
   const int jp = tid % kPairs, pg = tid / kPairs;
+  auto vrow = [&](int i) -> const __half* { return i == p ? vn : vcm + (size_t)i * d; };
   float ax = 0.0f, ay = 0.0f;
   int i = pg;
   for (; i + 15 * kGroups < n; i += 16 * kGroups) {
     __half2 v[16];
 #pragma unroll
-    for (int u = 0; u < 16; u++) v[u] = *reinterpret_cast<const __half2*>(vcm + (size_t)(i + u * kGroups) * d + 2 * jp);
+    for (int u = 0; u < 16; u++) v[u] = *reinterpret_cast<const __half2*>(vrow(i + u * kGroups) + 2 * jp);
 #pragma unroll
     for (int u = 0; u < 16; u++) {
       const float2 f = __half22float2(v[u]);
@@ -180,7 +203,7 @@ __global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* 
     }
   }
   for (; i < n; i += kGroups) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vcm + (size_t)i * d + 2 * jp));
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vrow(i) + 2 * jp));
     ax = fmaf(sc[i], f.x, ax);
     ay = fmaf(sc[i], f.y, ay);
   }
