@@ -78,6 +78,8 @@ struct GemvShape {
   static constexpr int kRedFloats = 4 * R;         // per lane
   static constexpr int kRed = 2 * kGemvWarps * 32 * kRedFloats * 4;
   static constexpr int kRedCta = kGemvMaxTilesCta * 32 * kRedFloats * 4;
+  // one-token partials of up to kGemvMaxTilesCta tiles (8 lanes x 2R floats per warp)
+  static_assert(kGemvMaxTilesCta * kGemvWarps * 8 * 2 * R * 4 <= kRed, "deferred partials exceed the reduction area");
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -307,6 +309,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
   cp_async_wait<0>();
   __syncthreads();
 
+  // One token row and one CTA per tile range: no barrier per tile.  Each
+  // warp's partial sums of every tile are kept (2R floats for each of the 8
+  // lanes of token column 0, at most 16 tiles: within the double-buffered
+  // reduction area) and reduced after the last tile, in the same fixed order.
+  const bool defer = a.M == 1 && C == 1 && ntl <= kGemvMaxTilesCta;
   // lanes of token columns >= M read row 0: their MMA columns are never stored
   const uint32_t xrow = xs_base + (uint32_t)((g < a.M ? g : 0) * a.x_stride) * 2 + (uint32_t)(16 * t);
   int cs_slot = 0;
@@ -386,6 +393,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
       issue_next();
     }
 
+    if (defer) {
+      // one token: only lanes of token column 0 (t == 0) hold outputs; their
+      // partials wait in shared memory until every tile of the CTA is done
+      if (t == 0) {
+        float* mine = red + ((jl * kGemvWarps + warp) * 8 + g) * (2 * R);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          mine[2 * r] = acc[r][0];
+          mine[2 * r + 1] = acc[r][2];
+        }
+      }
+      continue;
+    }
     // deposit this warp's partial, reduce the 8 warps' partials in a fixed order
     float* mine = red + (((jl & 1) * kGemvWarps + warp) * 32 + lane) * S::kRedFloats;
 #pragma unroll
@@ -422,6 +442,36 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_stream_kernel(const Gemv
         }
         gemv_store_tile<R>(a, tot, bia, (q + jl * tstep) * TR, g, t);
       }
+    }
+  }
+
+  if (defer) {
+    bar_sync_warps(1, kGemvThreads);
+    for (int jl = warp; jl < ntl; jl += kGemvWarps) {
+      float tot[R][4];
+#pragma unroll
+      for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) tot[r][e] = 0.0f;
+      if (t == 0) {
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; w++) {
+          const float* pp = red + ((jl * kGemvWarps + w) * 8 + g) * (2 * R);
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            tot[r][0] += pp[2 * r];
+            tot[r][2] += pp[2 * r + 1];
+          }
+        }
+      }
+      float bia[R][2];
+      if (jl == pre_tile) {
+#pragma unroll
+        for (int r = 0; r < R; r++) { bia[r][0] = bias_pre[r][0]; bia[r][1] = bias_pre[r][1]; }
+      } else {
+        gemv_load_bias<R>(a, bia, (q + jl * tstep) * TR, g);
+      }
+      gemv_store_tile<R>(a, tot, bia, (q + jl * tstep) * TR, g, t);
     }
   }
 
