@@ -23,6 +23,9 @@
 //               A from TMEM, B = X tile from shared memory, f32 accumulator in TMEM);
 //               tcgen05.commit releases operand stages and
 //               hands finished accumulators to the epilogue
+//   warp 14     (64-token tiles only) a second issuer: it takes the stages of
+//               dequant warpgroup 1 into a second accumulator, which the
+//               epilogue adds to the first
 //   warps 10-13 epilogue: tcgen05.ld of one of two TMEM accumulators (so the next
 //               tile's MMAs overlap this tile's stores), alpha/bias/beta, f16/f32 store
 // Operand stages (128 k: one code group) are an mbarrier ring (STAGES deep); the
@@ -126,9 +129,21 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// v[i] += u[i] as f32 (the two issuers' accumulators of one unit)
+template <int N>
+__device__ __forceinline__ void add_f32_regs(uint32_t (&v)[N], const uint32_t (&u)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(u[i]));
+}
 
-template <int LAYOUT, int BT, int STAGES, int NACC>
-__global__ void __launch_bounds__(kTcThreads, 1)
+// ISS MMA-issuing threads (warp 9, and warp 14 when ISS = 2).  One thread
+// issues a tcgen05.mma about every 67 cycles whatever N, while a 128 x 64 x 16
+// MMA holds 32 cycles of tensor work; two threads issuing into separate
+// accumulators reach one MMA per ~37 cycles (measured on B200, back-to-back
+// MMAs).  With ISS = 2, issuer w takes the 128-k groups of dequant warpgroup w
+// (G % 2 == w) into its own accumulator, and the epilogue adds the two.
+template <int LAYOUT, int BT, int STAGES, int NACC, int ISS>
+__global__ void __launch_bounds__(kTcThreads + 32 * (ISS - 1), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
                    const TcArgs a, int n_tiles, int num_tiles) {
   using L = TcSmem<BT, STAGES>;
@@ -146,12 +161,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // BT = 192 and NACC = 2 one A slot per warpgroup remains: a warpgroup then
   // dequantises group G + 2 while the MMAs of the other warpgroup's group G + 1
   // run, which at 192 tokens take longer than the dequantisation.
-  constexpr int kFreeCols = 512 - NACC * BT;
+  static_assert(ISS == 1 || ISS == 2, "one or two MMA issuers");
+  constexpr int kAccCols = NACC * ISS * BT;  // accumulator buf, issuer w at column (buf * ISS + w) * BT
+  constexpr int kFreeCols = 512 - kAccCols;
   constexpr int kASlots = kFreeCols / kAStageCols >= 8 ? 8 : (kFreeCols / kAStageCols) & ~1;
   static_assert(kASlots >= 2, "one A slot per dequant warpgroup at least");
   constexpr int kAPer = kASlots / 2;
-  constexpr uint32_t kAColBase = NACC * BT;  // A stages follow the accumulators
-  constexpr uint32_t kNeed = NACC * BT + kASlots * kAStageCols;
+  constexpr uint32_t kAColBase = kAccCols;  // A stages follow the accumulators
+  constexpr uint32_t kNeed = kAccCols + kASlots * kAStageCols;
   constexpr uint32_t kCols = kNeed <= 32 ? 32 : kNeed <= 64 ? 64 : kNeed <= 128 ? 128 : kNeed <= 256 ? 256 : 512;
   static_assert(kNeed <= 512, "TMEM budget");
   static_assert(kAColBase + kASlots * kAStageCols <= kCols, "A stages inside the allocation");
@@ -165,8 +182,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* empty_a = full_a + kASlots;  // [kASlots]
   uint64_t* acc_full = empty_a + kASlots;  // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2]
-  uint64_t* mma_drain = acc_empty + 2;     // [1] error path: completion of every issued MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
+  uint64_t* mma_drain = acc_empty + 2;     // [ISS] error path: completion of every issued MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + ISS);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   // A wait that runs out records its code and raises abort_flag; every other
   // wait of the CTA then returns at once (its phase can no longer complete),
@@ -189,10 +206,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::mbar_init(&empty_a[s], 1);
     }
     for (int b = 0; b < 2; b++) {
-      tc::mbar_init(&acc_full[b], 1);
-      tc::mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      tc::mbar_init(&acc_full[b], ISS);  // one commit per issuer
+      tc::mbar_init(&acc_empty[b], 4);   // one arrival per epilogue warp
     }
-    tc::mbar_init(mma_drain, 1);
+    for (int w = 0; w < ISS; w++) tc::mbar_init(&mma_drain[w], 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -248,8 +265,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int i = (it > STAGES ? it - STAGES : 0); i < it; i++)
         tc::mbar_wait(&full_x[i % STAGES], (i / STAGES) & 1);
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 9 || (ISS == 2 && warp == 14)) {
+    // ------------------------------------------------------------ MMA issuer(s)
+    const int iw = warp == 9 ? 0 : 1;  // issuer index
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(128, BT);
       // The issuing thread's per-stage work is the MMA pipe's throughput limit
@@ -275,12 +293,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
         tc::tc_fence_after();
-        const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT);
+        const uint32_t tmem_d = tmem_base + (uint32_t)((buf * ISS + iw) * BT);
         int tile, split, g0, g1;
         tc_unit(a, blockIdx.x + j * gridDim.x, a.Kp >> 7, tile, split, g0, g1);
 #pragma unroll 2
         for (int G = g0; G < g1; G++) {
           const int w = G & 1;  // warpgroup that dequantised this stage
+          if (ISS == 2 && w != iw) {  // the other issuer's stage: only keep the X ring position
+            if (++xslot == STAGES) { xslot = 0; xph ^= 1u; }
+            continue;
+          }
           const int as = w ? kAPer + aslot1 : aslot0;
           const uint32_t aph = w ? aph1 : aph0;
           if (w) {
@@ -303,7 +325,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int kk = 0; kk < kStageK / 16; kk++)
             tc::umma_f16_ta(tmem_d, at + (uint32_t)(kk * 8),
                             bdesc + (uint64_t)(((kk >> 2) * L::kXTile + (kk & 3) * 32) >> 4), idesc,
-                            (G > g0 || kk > 0) ? 1u : 0u);
+                            (G >= g0 + ISS || kk > 0) ? 1u : 0u);
           tc::umma_commit(&empty_x[xslot]);
           tc::umma_commit(&empty_a[as]);
           if (++xslot == STAGES) { xslot = 0; xph ^= 1u; }
@@ -313,8 +335,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!ok) {
         // no MMA issued by this thread may still write tensor memory when the CTA
         // frees it: wait (bounded) for all of them
-        tc::umma_commit(mma_drain);
-        tc::mbar_wait(mma_drain, 0);
+        tc::umma_commit(&mma_drain[iw]);
+        tc::mbar_wait(&mma_drain[iw], 0);
       }
     }
   } else if (warp < 8) {
@@ -499,7 +521,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::tc_fence_after();
       const bool row_ok = n < a.N;
       const float bias = (a.bias && row_ok) ? __half2float(a.bias[n]) : 0.0f;
-      const uint32_t tmem_d = tmem_base + (uint32_t)(buf * BT) + ((uint32_t)(q * 32) << 16);
+      // accumulators of this unit: with two issuers, issuer w's holds the groups
+      // G % 2 == w (absent when the unit has a single group of the other parity);
+      // the epilogue reads the first present one and adds the second
+      const uint32_t tmem_d0 = tmem_base + (uint32_t)(buf * ISS * BT) + ((uint32_t)(q * 32) << 16);
+      const bool has0 = ISS == 1 || g1 - g0 >= 2 || (g0 & 1) == 0;
+      const bool add2 = ISS == 2 && has0 && g1 - g0 >= 2;
+      const uint32_t tmem_d = has0 ? tmem_d0 : tmem_d0 + (uint32_t)BT;
+      const uint32_t tmem_d2 = tmem_d0 + (uint32_t)BT;
       if (a.splits == 1 && a.tma_epi != kEpiThreads) {
         // Staged epilogue.  Per chunk of tokens the warp reads its 32 rows in
         // the mma-fragment layout (16x256b: thread (g, t4) holds rows g, g + 8
@@ -536,7 +565,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               uint32_t v[2][8];
               tc::tmem_ld_16x256b_x2(tmem_d + (uint32_t)(c * 32 + hh * 16), v[0]);
               tc::tmem_ld_16x256b_x2(tmem_d + (16u << 16) + (uint32_t)(c * 32 + hh * 16), v[1]);
-              tc::tmem_ld_wait();
+              if (ISS == 2 && add2) {
+                uint32_t u[2][8];
+                tc::tmem_ld_16x256b_x2(tmem_d2 + (uint32_t)(c * 32 + hh * 16), u[0]);
+                tc::tmem_ld_16x256b_x2(tmem_d2 + (16u << 16) + (uint32_t)(c * 32 + hh * 16), u[1]);
+                tc::tmem_ld_wait_regs(u[0], u[1]);
+                tc::reg_tie(v[0]);
+                tc::reg_tie(v[1]);
+                add_f32_regs(v[0], u[0]);
+                add_f32_regs(v[1], u[1]);
+              } else {
+                tc::tmem_ld_wait();
+              }
 #pragma unroll
               for (int h = 0; h < 2; h++)
 #pragma unroll
@@ -597,7 +637,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               uint32_t v[2][4];
               tc::tmem_ld_16x256b_x1(tmem_d + (uint32_t)(c * 16 + hh * 8), v[0]);
               tc::tmem_ld_16x256b_x1(tmem_d + (16u << 16) + (uint32_t)(c * 16 + hh * 8), v[1]);
-              tc::tmem_ld_wait();
+              if (ISS == 2 && add2) {
+                uint32_t u[2][4];
+                tc::tmem_ld_16x256b_x1(tmem_d2 + (uint32_t)(c * 16 + hh * 8), u[0]);
+                tc::tmem_ld_16x256b_x1(tmem_d2 + (16u << 16) + (uint32_t)(c * 16 + hh * 8), u[1]);
+                tc::tmem_ld_wait_regs(u[0], u[1]);
+                tc::reg_tie(v[0]);
+                tc::reg_tie(v[1]);
+                add_f32_regs(v[0], u[0]);
+                add_f32_regs(v[1], u[1]);
+              } else {
+                tc::tmem_ld_wait();
+              }
 #pragma unroll
               for (int h = 0; h < 2; h++)
 #pragma unroll
@@ -628,7 +679,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int cc = 0; cc < BT / 32; cc++) {
           uint32_t v[32];
           tc::tmem_ld_32x32b_x32(tmem_d + (uint32_t)(cc * 32), v);
-          tc::tmem_ld_wait();
+          if (ISS == 2 && add2) {
+            uint32_t u[32];
+            tc::tmem_ld_32x32b_x32(tmem_d2 + (uint32_t)(cc * 32), u);
+            tc::tmem_ld_wait();
+            tc::reg_tie(u);
+            tc::reg_tie(v);
+            add_f32_regs(v, u);
+          } else {
+            tc::tmem_ld_wait();
+          }
           const int tok0 = m0 + cc * 32;
           if (!row_ok || tok0 >= a.M) continue;
           const int ntok = min(32, a.M - tok0);
@@ -647,7 +707,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int cc = 0; cc < BT / 32; cc++) {
           uint32_t v[32];
           tc::tmem_ld_32x32b_x32(tmem_d + (uint32_t)(cc * 32), v);
-          tc::tmem_ld_wait();
+          if (ISS == 2 && add2) {
+            uint32_t u[32];
+            tc::tmem_ld_32x32b_x32(tmem_d2 + (uint32_t)(cc * 32), u);
+            tc::tmem_ld_wait();
+            tc::reg_tie(u);
+            tc::reg_tie(v);
+            add_f32_regs(v, u);
+          } else {
+            tc::tmem_ld_wait();
+          }
 #pragma unroll
           for (int jj = 0; jj < 32; jj++) part[(size_t)(cc * 32 + jj) * 128 + rr] = __uint_as_float(v[jj]);
         }
@@ -747,7 +816,7 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-template <int LAYOUT, int BT, int STAGES, int NACC>
+template <int LAYOUT, int BT, int STAGES, int NACC, int ISS>
 static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaStream_t st, bool pdl) {
   using L = TcSmem<BT, STAGES>;
   EncodeTiledFn enc = get_encode_fn();
@@ -775,7 +844,7 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   }
-  auto kern = gemm_tc_kernel<LAYOUT, BT, STAGES, NACC>;
+  auto kern = gemm_tc_kernel<LAYOUT, BT, STAGES, NACC, ISS>;
   // the shared-memory opt-in is a per-device property of the kernel: set it once
   // on every device this instance runs on (idempotent; a racing second set is harmless)
   static bool attr_set[kTcMaxDevices] = {};
@@ -793,7 +862,7 @@ static cudaError_t launch_tc_t(const TcArgs& a, const __half* x, int ldx, cudaSt
   const int num_tiles = n_tiles * ((a.M + BT - 1) / BT) * a.splits;  // work units
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_tiles < num_sms ? num_tiles : num_sms);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3(kTcThreads + 32 * (ISS - 1));
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -847,7 +916,7 @@ constexpr int kTcEpiCyclesPerToken = 60;
 
 static TcPlan plan_tc(int K, int N, int M, int sms, size_t ws_avail, int epi_per_token = kTcEpiCyclesPerToken) {
   struct Cand { int bt, nacc; };
-  const Cand cands[] = {{64, 2}, {128, 2}, {192, 1}, {224, 1}, {256, 1}, {192, 2}};
+  const Cand cands[] = {{64, 1}, {128, 2}, {192, 1}, {224, 1}, {256, 1}, {192, 2}};
   const int splits_c[] = {1, 2, 3, 4, 6, 8};  // the reduction unrolls up to 8 slices
   const long long n_tiles = (N + 127) / 128;
   const int KG = padded_k(K) / 128;
@@ -924,21 +993,21 @@ cudaError_t launch_gemm_tc(const uint8_t* tiled, int layout, int K, int N, const
   }
   if (layout == 1) {
     switch (p.bt) {
-      case 64: return launch_tc_t<1, 64, 4, 2>(a, x, ldx, st, pdl);
-      case 128: return launch_tc_t<1, 128, 3, 2>(a, x, ldx, st, pdl);
-      case 192: return p.nacc == 2 ? launch_tc_t<1, 192, 3, 2>(a, x, ldx, st, pdl)
-                                   : launch_tc_t<1, 192, 3, 1>(a, x, ldx, st, pdl);
-      case 224: return launch_tc_t<1, 224, 2, 1>(a, x, ldx, st, pdl);
-      default: return launch_tc_t<1, 256, 2, 1>(a, x, ldx, st, pdl);
+      case 64: return launch_tc_t<1, 64, 6, 1, 2>(a, x, ldx, st, pdl);
+      case 128: return launch_tc_t<1, 128, 3, 2, 1>(a, x, ldx, st, pdl);
+      case 192: return p.nacc == 2 ? launch_tc_t<1, 192, 3, 2, 1>(a, x, ldx, st, pdl)
+                                   : launch_tc_t<1, 192, 3, 1, 1>(a, x, ldx, st, pdl);
+      case 224: return launch_tc_t<1, 224, 2, 1, 1>(a, x, ldx, st, pdl);
+      default: return launch_tc_t<1, 256, 2, 1, 1>(a, x, ldx, st, pdl);
     }
   }
   switch (p.bt) {
-    case 64: return launch_tc_t<0, 64, 4, 2>(a, x, ldx, st, pdl);
-    case 128: return launch_tc_t<0, 128, 3, 2>(a, x, ldx, st, pdl);
-    case 192: return p.nacc == 2 ? launch_tc_t<0, 192, 3, 2>(a, x, ldx, st, pdl)
-                                 : launch_tc_t<0, 192, 3, 1>(a, x, ldx, st, pdl);
-    case 224: return launch_tc_t<0, 224, 2, 1>(a, x, ldx, st, pdl);
-    default: return launch_tc_t<0, 256, 2, 1>(a, x, ldx, st, pdl);
+    case 64: return launch_tc_t<0, 64, 6, 1, 2>(a, x, ldx, st, pdl);
+    case 128: return launch_tc_t<0, 128, 3, 2, 1>(a, x, ldx, st, pdl);
+    case 192: return p.nacc == 2 ? launch_tc_t<0, 192, 3, 2, 1>(a, x, ldx, st, pdl)
+                                 : launch_tc_t<0, 192, 3, 1, 1>(a, x, ldx, st, pdl);
+    case 224: return launch_tc_t<0, 224, 2, 1, 1>(a, x, ldx, st, pdl);
+    default: return launch_tc_t<0, 256, 2, 1, 1>(a, x, ldx, st, pdl);
   }
 }
 

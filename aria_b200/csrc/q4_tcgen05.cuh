@@ -242,6 +242,13 @@ __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&a)[8], uint32_t (&b
                :
                : "memory");
 }
+// Placed after tmem_ld_wait: ties registers of completed loads to that point
+// (asm statements keep their order), so no use of them moves above the wait.
+template <int N>
+__device__ __forceinline__ void reg_tie(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&a)[4], uint32_t (&b)[4]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3])
