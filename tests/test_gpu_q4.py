@@ -132,6 +132,23 @@ def test_odd_shapes(q4, coracle, layout, K, N, M):
     check_close(y, ref, what=f"odd {layout} {K}x{N} M={M}")
 
 
+@pytest.mark.parametrize("layout,K,N,M", [(LAYOUT_KN, 32, 1056, 64), (LAYOUT_KN, 128, 1056, 33),
+                                          (LAYOUT_KN, 256, 1056, 64), (LAYOUT_KN, 384, 2048, 48),
+                                          (LAYOUT_NK, 128, 1057, 64), (LAYOUT_NK, 640, 1301, 40),
+                                          (LAYOUT_KN, 4096, 2048, 64)])
+def test_tensor_path_group_parities(q4, coracle, layout, K, N, M):
+    """64-token tiles take two MMA issuers, each accumulating the 128-k groups of
+    one parity; the epilogue adds both, or reads the only one present when a
+    work unit holds a single group.  Units of one, two and three groups, odd N
+    (NK), and a K split, all on the tensor-core kernel."""
+    from aria_b200 import _lib
+    lib = _lib.lib()
+    ws = int(lib.aria_q4_0_workspace_bytes(K, N, M))
+    assert lib.aria_q4_0_kernel_choice(layout, K, N, M, ws, 0) == 3
+    y, ref = _run(q4, coracle, layout, K, N, M, out_dtype=torch.float16, bias=True)
+    check_close(y, ref, what=f"tensor {layout} {K}x{N} M={M}")
+
+
 def test_alpha_beta(q4, coracle):
     y, ref = _run(q4, coracle, LAYOUT_KN, 896, 896, 2, alpha=0.5, beta=0.25)
     check_close(y, ref, what="alpha/beta")
