@@ -632,7 +632,11 @@ static int gemv_max_clusters(int layout, int R, int P, int C, int per_sm, int sm
 //     (x1.4 when two CTAs share an SM)
 //   + 300 per row tile of a CTA (partial-sum reduction and store)
 //   + 20 per token row and 128-k group of activations staged per SM (the
-//     prologue copies them from L2 before the weight stream starts)
+//     prologue copies them from L2 before the weight stream starts); 8 for a
+//     single row (refit at M = 1 after the per-tile barrier was removed: the
+//     chosen plan is within 0.3% of the fastest of every feasible plan on the
+//     Efkolos ffn_down / LM head and config-4 attn_out / ffn_down / QKV / LM
+//     head, against 2% with 20 -- config-4 attn_out 4.76 -> 4.33 us)
 //   + 3000 for a cluster split (cluster barriers, distributed-shared-memory sums).
 // Time is set by each warp's chain of chunk arrival -> dequantisation -> MMA ->
 // scale FMAs (without the arithmetic the same copies stream ~1.8x faster), so the
@@ -659,8 +663,9 @@ static bool plan_gemv(int layout, int K, int N, int M, int sms, GemvPlan& best) 
                                      : (P == 2 ? gemv_smem<1, 2>(C, xbytes, chunks) : gemv_smem<1, 1>(C, xbytes, chunks));
           if (smem > (per_sm == 2 ? kGemvSmemHalf : kGemvSmemMax)) continue;
           const int ctas_per_sm = std::min(per_sm, (clusters * C + sms - 1) / sms);
+          const long long x_cost = M == 1 ? 8 : 20;
           const long long cost = chunks * (100 + 150 * R * P) * (per_sm == 2 ? 7 : 5) / 5 + 300LL * tpc +
-                                 20LL * ctas_per_sm * M * gmax + (C > 1 ? 3000 : 0);
+                                 x_cost * ctas_per_sm * M * gmax + (C > 1 ? 3000 : 0);
           if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             best.R = R;

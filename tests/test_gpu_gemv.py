@@ -122,6 +122,41 @@ def test_kernel_flags_errors(q4):
     torch.cuda.synchronize()
 
 
+@pytest.mark.parametrize("layout,K,N", [(LAYOUT_KN, 4096, 16384), (LAYOUT_NK, 4096, 31500), (LAYOUT_KN, 3584, 896)])
+def test_chained_launches_bit_identical(q4, layout, K, N):
+    """One token through a CUDA graph of back-to-back launches over four copies
+    of the weight (programmatic dependent launch, const-weights flag: each
+    launch streams its first chunks while the previous one runs), every launch
+    into its own NaN-filled output: every output of every launch must equal a
+    single standalone launch's bits (no unwritten element, no dependence on a
+    neighbouring launch)."""
+    g_ = torch.Generator(device="cuda")
+    g_.manual_seed(K + N)
+    shape = (K, N) if layout == LAYOUT_KN else (N, K)
+    w0 = q4.Q4Weight.from_f16((torch.randn(shape, generator=g_, device="cuda") * 0.02).half(), layout)
+    pool = [w0] + [q4.Q4Weight(w0.buf.clone(), layout, K, N) for _ in range(3)]
+    x = torch.randn(1, K, generator=g_, device="cuda").half()
+    ref = torch.empty(1, N, dtype=torch.float16, device="cuda")
+    s = torch.cuda.Stream()
+    ys = [torch.empty(1, N, dtype=torch.float16, device="cuda") for _ in range(16)]
+    s.wait_stream(torch.cuda.current_stream())  # the weights and inputs were made on the current stream
+    with torch.cuda.stream(s):
+        q4.matmul(x, w0, ref, const_weights=True, kernel="stream")
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for j, y in enumerate(ys):
+                q4.matmul(x, pool[j % 4], y, const_weights=True, kernel="stream")
+        for _ in range(5):
+            for y in ys:
+                y.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize()
+            for j, y in enumerate(ys):
+                assert torch.equal(y, ref), f"launch {j}"
+    del graph
+
+
 def test_no_device_error_recorded(q4):
     from aria_b200 import _lib
     assert _lib.lib().aria_q4_take_device_error() == 0
