@@ -95,7 +95,8 @@ def test_embed_kernel_clamps():
 
 
 @pytest.mark.parametrize("layout,K,N,M", [(0, 896, 2688, 1), (0, 896, 3584, 5), (0, 4096, 1024, 16),
-                                          (1, 896, 1000, 40), (0, 256, 512, 64)])
+                                          (1, 896, 1000, 40), (0, 256, 512, 64), (1, 896, 2048, 3),
+                                          (0, 800, 1024, 2), (0, 896, 896, 8), (0, 4096, 4096, 1)])
 def test_layernorm_prologue(coracle, layout, K, N, M):
     """aria_q4_0_matmul_ln against the fp64 oracle of LayerNorm (rounded to f16,
     as the projection reads it) followed by the projection, with bias and the
