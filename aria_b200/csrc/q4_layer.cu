@@ -182,6 +182,10 @@ __global__ void __launch_bounds__(kLayerThreads) attention_kernel(const __half* 
     sum += e;
   }
   sum = block_sum(sum, red);  // its barriers also publish sc[]
+  // the scores are done: let the next kernel (attn_out, launched with
+  // programmatic dependence) start loading its weights while the weighted sum
+  // of V runs; it still waits for this grid to complete before reading out
+  grid_dep_launch();
   const float inv = 1.0f / sum;
   // weighted sum of V: thread = (dimension pair jp, position group pg); up to
   // 16 positions' pairs loaded before their multiply-adds
