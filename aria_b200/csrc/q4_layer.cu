@@ -55,6 +55,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 __global__ void __launch_bounds__(kLayerThreads) embed_kernel(const __half* embed, const __half* pos_embed,
                                                               const int* tok, const int* pos, int vocab, int max_seq,
                                                               int d, float* h) {
+  grid_dep_launch();  // the next projection (programmatic dependence) may load its weights meanwhile
   const int m = blockIdx.x;
   const int tk = min(max(tok[m], 0), vocab - 1), ps = min(max(pos[m], 0), max_seq - 1);
   const __half* e = embed + (size_t)tk * d;
@@ -242,6 +243,7 @@ template <int V4>
 __global__ void __launch_bounds__(kLayerThreads) layernorm_warp_kernel(const float* x, const __half* g,
                                                                        const __half* b, int M, int d, float eps,
                                                                        __half* y, int ldy) {
+  grid_dep_launch();  // the next projection (programmatic dependence) may load its weights meanwhile
   const int row = (int)blockIdx.x * (kLayerThreads / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
   const int n4 = d >> 2;
